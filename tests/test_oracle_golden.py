@@ -1,0 +1,121 @@
+"""Pin the C restatement (oracle/kz_oracle.c) to the reference's own outputs.
+
+The fixtures were produced by the reference's unmodified Python running over
+its own compiled C++ core (tests/golden/gen_golden.py).  Integer codes must be
+bit-exact; scales must be the identical double; dequantized and fp32 matmul
+outputs must be bit-identical fp32.
+"""
+import numpy as np
+import pytest
+
+import inputs
+from conftest import golden
+from oracle import cpu as ocpu
+
+
+@pytest.fixture(scope="module")
+def qcases():
+    g = golden("quantize_cases.npz")
+    cases = inputs.quantize_case_inputs()
+    return g, cases
+
+
+def test_quantize_inputs_match_fixture_hashes(qcases):
+    g, cases = qcases
+    for name, x in cases.items():
+        assert inputs.sha(x) == str(g[f"{name}__x_sha256"]), name
+
+
+def test_quantize_tensor_bit_exact_vs_reference(qcases):
+    g, cases = qcases
+    for name, x in cases.items():
+        q, s = ocpu.quantize_tensor(x)
+        assert s == float(g[f"{name}__scale"]), name
+        np.testing.assert_array_equal(q, g[f"{name}__q"], err_msg=name)
+        assert q.min() >= -127 and q.max() <= 127
+
+
+def test_dequantize_bit_exact_vs_reference(qcases):
+    g, cases = qcases
+    for name in cases:
+        if f"{name}__deq" not in g:
+            continue
+        deq = ocpu.dequantize(g[f"{name}__q"], float(g[f"{name}__scale"]))
+        assert deq.tobytes() == g[f"{name}__deq"].astype(np.float32).tobytes(), name
+
+
+def test_reference_properties_test_quantize_py(qcases):
+    """tests/test_quantize.py:41-72 restated on the oracle."""
+    g, cases = qcases
+    x = cases["uniform1000"]
+    q, s = ocpu.quantize_tensor(x)
+    err = np.abs(x.astype(np.float64) - ocpu.dequantize(q, s).astype(np.float64)).max()
+    assert err <= s / 2 + 1e-6
+    q0, _ = ocpu.quantize_tensor(cases["zero_one"])
+    assert q0[0] == 0
+    assert int(g["randn256_seed1__nbytes"]) * 4 == 4 * 65536
+
+
+def test_nonfinite_raises():
+    for bad in (np.float32(np.nan), np.float32(np.inf), np.float32(-np.inf)):
+        with pytest.raises(ValueError):
+            ocpu.quantize_tensor(np.asarray([1.0, bad, 2.0], np.float32))
+
+
+def test_percol_matches_reference_columnwise():
+    g = golden("percol_cases.npz")
+    w = inputs.percol_weight()
+    assert inputs.sha(w) == str(g["w_sha256"])
+    qT, s = ocpu.quantize_cols(w)
+    np.testing.assert_array_equal(qT, g["qT"])
+    np.testing.assert_array_equal(s, g["scales"])
+    assert s[3] == 1.0 and not qT[3].any()
+
+
+def test_qlinear_w8a32_bit_exact_vs_reference():
+    g = golden("w8a32_cases.npz")
+    for i in range(int(g["count"])):
+        x, w, b = inputs.w8a32_inputs(i)
+        assert inputs.sha(x) + inputs.sha(w) + inputs.sha(b) == str(g[f"c{i}__inputs_sha256"])
+        q, s = ocpu.quantize_tensor(w)
+        np.testing.assert_array_equal(q, g[f"c{i}__q"])
+        assert s == float(g[f"c{i}__scale"])
+        for act, key in ((0, "y"), (1, "y_relu")):
+            y = ocpu.qlinear_w8a32(x, q, s, b, act=act)
+            assert y.tobytes() == g[f"c{i}__{key}"].tobytes(), (i, key)
+        # gelu goes through erff, identical libm here
+        y = ocpu.qlinear_w8a32(x, q, s, b, act=2)
+        np.testing.assert_allclose(y, g[f"c{i}__y_gelu"], rtol=0, atol=1e-6)
+
+
+def test_mlp_config1_vs_reference():
+    g = golden("mlp_config1.npz")
+    x, b1, b2 = inputs.mlp_config1_inputs()
+    assert inputs.sha(x) == str(g["x_sha256"])
+    h = ocpu.qlinear_w8a32(x, g["q1"], float(g["s1"]), b1, act=1)
+    assert h.tobytes() == g["h"].tobytes()
+    y = ocpu.qlinear_w8a32(h, g["q2"], float(g["s2"]), b2, act=0)
+    assert y.tobytes() == g["y"].tobytes()
+
+
+def test_xor_qlinear_vs_reference():
+    g = golden("xor_qlinear.npz")
+    q1, s1 = ocpu.quantize_tensor(g["w1"])
+    q2, s2 = ocpu.quantize_tensor(g["w2"])
+    h = ocpu.qlinear_w8a32(g["x"], q1, s1, g["b1"], act=1)
+    y = ocpu.qlinear_w8a32(h, q2, s2, g["b2"], act=0)
+    assert y.tobytes() == g["quant_preds"].tobytes()
+    assert [round(float(v)) for v in y.ravel()] == [0, 1, 1, 0]
+
+
+def test_int8_gemm_and_epilogue_small():
+    rs = np.random.RandomState(1)
+    a = rs.randint(-127, 128, (33, 80)).astype(np.int8)
+    b = rs.randint(-127, 128, (17, 80)).astype(np.int8)
+    acc = ocpu.gemm_i8(a, b)
+    np.testing.assert_array_equal(acc, a.astype(np.int64) @ b.astype(np.int64).T)
+    rsc = rs.uniform(1e-3, 1e-2, 33)
+    csc = rs.uniform(1e-3, 1e-2, 17)
+    y = ocpu.epilogue(acc, rsc, csc)
+    ref = (acc.astype(np.float32) * rsc.astype(np.float32)[:, None]).astype(np.float32) * csc.astype(np.float32)[None, :]
+    assert y.tobytes() == ref.astype(np.float32).tobytes()
