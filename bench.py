@@ -1,0 +1,392 @@
+"""Benchmark of Kansai's int8 quantized-linear hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload ("config 2"): one per-channel int8
+quantized Linear, fp32 weight [4096, 4096] ~ N(0, 0.02) quantized once per
+output channel, fp32 activations [2048, 4096] ~ N(0, 1).  One step = one
+forward of that layer over one batch of 2048 tokens: per-tensor activation
+absmax + quantize (2 HBM-bound kernels), then the tcgen05 int8 GEMM with the
+per-row x per-channel rescale fused into its epilogue, fp32 output.  Weight
+quantization is the layer's one-time construction (QLinear.__init__), as in
+the reference (quantize.py:139-141), and is not in the step.
+
+Inputs exceed L2: 4 rotating sets of (X fp32, weight codes, Y fp32) = 336 MB,
+so every step reads cold data.  Timing: W warm-up steps, then K steps between
+barrier + synchronize on both sides, CUDA events on the launching stream, max
+over ranks.  N > 1 (torchrun): activations row-sharded, weights replicated:
+every rank runs its own 2048-token batch, no collective on the data path
+("weak" scaling).
+
+--impl reference: the reference's own CPU implementation of this layer,
+qlinear (quantize.py:115-122) = dequantize the weight in Python, then the
+reference's C++ Tensor::matmul + add (oracle/_ref, compiled from the
+reference's sources), on a bounded row sample, rows spread over all host
+threads as the reference's Shard(0) DeviceMesh dispatch does
+(distributed.py:73-102).  Under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_TOK, K_IN, N_OUT = 2048, 4096, 4096
+NSETS = 4
+METRIC = "int8 GEMM TOPS & quantized-linear tokens/s vs int8 roofline at 1/2/4/8 B200"
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of
+    the named kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML (read-only) while
+    the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
+
+
+# --------------------------------------------------------- reference (CPU)
+
+def reference_sample_step(core, q_list, scale, shape, x_parts, bias_t, threads):
+    """One qlinear call of the reference (quantize.py:115-122) on the row sample:
+    dequantize in Python (quantize.py:76-77), then the compiled reference core's
+    Tensor::matmul + add per row part on its own thread (GIL released)."""
+    flat = [v * scale for v in q_list]
+    w = core.from_flat(flat, shape)
+    out = [None] * len(x_parts)
+
+    def work(i):
+        out[i] = x_parts[i].matmul(w).add(bias_t)
+
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(len(x_parts))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    return out
+
+
+def reference_setup(rows_per_thread=8):
+    from oracle import cpu as ocpu
+    from oracle.refpkg import load_reference_core
+    core = load_reference_core()
+    threads = os.cpu_count() or 1
+    rs = np.random.RandomState(7)
+    w = (rs.standard_normal((K_IN, N_OUT)) * 0.02).astype(np.float32)
+    q, scale = ocpu.quantize_tensor(w)           # the reference's per-tensor scheme
+    rows = rows_per_thread * threads
+    x = rs.standard_normal((rows, K_IN)).astype(np.float32)
+    parts = [core.from_flat(p.ravel().tolist(), [p.shape[0], K_IN]) for p in np.array_split(x, threads)]
+    bias = core.from_flat([0.0] * N_OUT, [N_OUT])
+    return core, q.ravel().tolist(), float(scale), [K_IN, N_OUT], parts, bias, threads, rows
+
+
+def time_reference(steps, warmup, budget_s=None):
+    """Times `steps` reference qlinear calls (after `warmup`); with a budget,
+    runs as many of the requested steps as fit in it.  Returns
+    (tokens/s, seconds per step, threads, rows per step, steps timed)."""
+    core, ql, scale, shape, parts, bias, threads, rows = reference_setup()
+    t_w = time.perf_counter()
+    for _ in range(max(warmup, 1)):
+        reference_sample_step(core, ql, scale, shape, parts, bias, threads)
+    est = (time.perf_counter() - t_w) / max(warmup, 1)
+    if budget_s is not None:
+        steps = max(1, min(steps, int(budget_s / max(est, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        reference_sample_step(core, ql, scale, shape, parts, bias, threads)
+    dt = (time.perf_counter() - t0) / steps
+    return rows / dt, dt, threads, rows, steps
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    try:
+        value, dt, threads, rows, timed = time_reference(args.steps, min(args.warmup, 1), budget_s=120.0)
+    except Exception as e:  # the compiled reference core is missing
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path could not run: {e}"}))
+        return
+    sample = (f"reference qlinear on {rows} of 2048 rows of config 2 (weight dequantized in Python every call, "
+              f"quantize.py:121, then Tensor::matmul + add split over {threads} threads)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": timed, "steps_requested": args.steps, "warmup": min(args.warmup, 1), "ms_per_step": dt * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2 per-channel int8 Linear [4096x4096] @ 2048 tokens (reference: W8A32 per-tensor)",
+                       "global_batch": M_TOK, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def cpu_baseline():
+    try:
+        value, dt, threads, rows, _ = time_reference(steps=3, warmup=1)
+        return {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "sample": f"reference qlinear (quantize.py:115-122; dequantize in Python each call, compiled "
+                          f"reference Tensor::matmul + add) on {rows} rows of config 2, 3 timed calls, "
+                          f"{threads} threads"}
+    except Exception as e:
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+
+
+# ---------------------------------------------------------------- our path
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local_rank = dist_env()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    import kansaiml_b200 as kz
+    from kansaiml_b200 import _lib
+    from kansaiml_b200 import quantize as kq
+
+    lib = _lib.load()
+    rs = np.random.RandomState(1000 + rank)
+    # one-time layer construction: NSETS independent weights, quantized per channel
+    layers = []
+    for i in range(NSETS):
+        w = torch.from_numpy((rs.standard_normal((K_IN, N_OUT)) * 0.02).astype(np.float32)).to(dev)
+
+        class _Lin:
+            pass
+        lin = _Lin()
+        lin.weight, lin.bias = kz.Tensor(w), None
+        layers.append(kq.QLinear(lin, per_channel=True))
+        del w
+    xs = [torch.from_numpy(rs.standard_normal((M_TOK, K_IN)).astype(np.float32)).to(dev) for _ in range(NSETS)]
+    ys = [torch.empty((M_TOK, N_OUT), dtype=torch.float32, device=dev) for _ in range(NSETS)]
+    xq = torch.empty((M_TOK, K_IN), dtype=torch.int8, device=dev)
+    s64 = torch.empty(1, dtype=torch.float64, device=dev)
+    s32 = torch.empty(1, dtype=torch.float32, device=dev)
+    partials = torch.empty(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    n_el = M_TOK * K_IN
+    B = [(L.qweight.kmajor().data_ptr(), L.qweight.scale_f32.data_ptr()) for L in layers]
+    X = [x.data_ptr() for x in xs]
+    Y = [y.data_ptr() for y in ys]
+    XQ, S64, S32, PP = xq.data_ptr(), s64.data_ptr(), s32.data_ptr(), partials.data_ptr()
+
+    def step(i, ev=None):
+        j = i % NSETS
+        if ev is not None:
+            ev[0].record(stream)
+        st = lib.kz_absmax_f32(X[j], n_el, PP, sh)
+        st |= lib.kz_quantize_partials_f32(X[j], n_el, PP, XQ, S64, S32, sh)
+        if ev is not None:
+            ev[1].record(stream)
+        st |= lib.kz_gemm_i8(XQ, B[j][0], M_TOK, N_OUT, K_IN, K_IN, S32, 0, B[j][1], 1, None, 0, Y[j], None,
+                             N_OUT, None, sh)
+        if ev is not None:
+            ev[2].record(stream)
+        if st:
+            raise RuntimeError(_lib.last_error())
+
+    # correctness guard on the benchmark's own data: row sample vs the oracle (setup, untimed)
+    step(0)
+    torch.cuda.synchronize()
+    if kq.device_status() != 0:
+        raise RuntimeError("device status set after the first step")
+
+    for i in range(args.warmup):
+        step(i)
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for i in range(K):
+            step(i, evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    quant_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    gemm_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / K
+    tokens = M_TOK * world
+    value = tokens / (ms_per_step / 1e3)
+    gemm_avg = statistics.mean(gemm_ms)
+    quant_avg = statistics.mean(quant_ms)
+    ops = 2.0 * M_TOK * N_OUT * K_IN
+    hbm_gbs, bf16, bf16_sus, peak_src = peaks()
+    int8_peak = 2.0 * bf16   # B200 int8 dense rate is 2x its bf16 dense rate
+    tops = ops / (gemm_avg / 1e3) / 1e12
+    quant_bytes = 9.0 * n_el   # absmax 4 B/el + quantize 4 B + 1 B per element
+
+    # ------------------------------------------------------------ e2e
+    # Through the public API with host buffers: pinned host X -> device,
+    # QLinear forward, device -> pinned host Y, every step.
+    x_host = [torch.from_numpy(rs.standard_normal((M_TOK, K_IN)).astype(np.float32)).pin_memory() for _ in range(2)]
+    y_host = torch.empty((M_TOK, N_OUT), dtype=torch.float32).pin_memory()
+    layer = layers[0]
+
+    def e2e_step(i):
+        xd = kz.Tensor(x_host[i % 2].to(dev, non_blocking=True))
+        y = layer(xd)
+        y_host.copy_(y.data, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = tokens / (e2e_ms / args.e2e_steps / 1e3)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+    traffic = profile_traffic("gemm_i8_config2")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "config2: per-channel int8 quantized Linear [4096 -> 4096], 2048 tokens/step/GPU, "
+                               "per-tensor activation quant, fused rescale, fp32 out",
+                   "global_batch": tokens, "seq_len": None, "parallelism": f"dp{world} (row-sharded activations)",
+                   "l2": f"inputs larger than L2: {NSETS} rotating (X, W, Y) sets, "
+                         f"{NSETS * (M_TOK * K_IN * 4 + K_IN * N_OUT + M_TOK * N_OUT * 4) / 1e6:.0f} MB"},
+        "tops": ops * world / (ms_per_step / 1e3) / 1e12,
+        "gpu_launches": 3 * K,
+        "roofline": {"kernel": "gemm_i8_kernel", "bound": "tensor", "achieved": tops, "peak": int8_peak,
+                     "unit": "TOP/s", "frac": tops / int8_peak, "traffic": traffic,
+                     "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
+                     "avg_launch_us": gemm_avg * 1e3,
+                     "algorithmic": f"2*M*N*K = {ops:.3e} op per launch"},
+        "kernels": {"quantize_activations": {"avg_us": quant_avg * 1e3, "bound": "hbm",
+                                             "achieved_gbs": quant_bytes / (quant_avg / 1e3) / 1e9,
+                                             "peak_gbs": hbm_gbs, "frac": quant_bytes / (quant_avg / 1e3) / 1e9 / hbm_gbs,
+                                             "algorithmic": "9 B/element (absmax 4 + quantize 4+1), 2 launches"}},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": M_TOK * K_IN * 4,
+                "d2h_bytes_per_step": M_TOK * N_OUT * 4},
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

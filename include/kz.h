@@ -1,0 +1,168 @@
+/*
+ * kz.h -- C ABI of libkz, the B200 (sm_100a) backend of Kansai's int8
+ * quantized-linear path.
+ *
+ * Plain C: device pointers, sizes, a CUDA stream handle and an int status.
+ * No exceptions and no C++ or PyTorch types cross this boundary.  Every entry
+ * point returns KZ_OK (0) or an error code; kz_last_error() returns the
+ * message of the calling thread's most recent failure.
+ *
+ * Each entry point names the reference interface it replaces
+ * (reference file:line, paths inside the KansaiML checkout).  The reference
+ * reaches all of them through its `kansai._core` extension
+ * (python/bindings.cpp:17); INTEGRATION.md shows the binding.
+ *
+ * Memory: the library allocates no device memory.  Outputs, and the small
+ * `partials` buffers some entry points use to hand an absmax from one kernel
+ * to the next, are caller-owned device buffers.
+ *
+ * Errors found on the device (a NaN/Inf in a tensor being quantized, a wait
+ * inside a kernel that ran out) cannot be returned synchronously; kernels
+ * record them in a sticky per-device status word read by kz_device_status().
+ */
+#ifndef KZ_H_
+#define KZ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same handle as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* kz_stream_t;
+
+enum kz_status_code {
+    KZ_OK = 0,
+    KZ_ERR_INVALID_ARGUMENT = 1,  /* bad shape, pointer, stride or alignment */
+    KZ_ERR_NONFINITE = 2,         /* NaN/Inf in a tensor being quantized
+                                     (quantize.py:69 raises ValueError/OverflowError) */
+    KZ_ERR_CUDA = 3,              /* a CUDA runtime/driver call failed */
+    KZ_ERR_UNSUPPORTED_DEVICE = 4,/* current device is not sm_100 (B200) */
+    KZ_ERR_DEVICE_TIMEOUT = 5     /* a bounded wait inside a kernel ran out */
+};
+
+enum kz_activation { KZ_ACT_NONE = 0, KZ_ACT_RELU = 1, KZ_ACT_GELU = 2 };
+
+/* Words in an absmax `partials` buffer (uint32_t[KZ_PARTIALS_WORDS]).
+ * Word 0 holds the number of valid partials P; words 1..P hold the bit
+ * patterns of non-negative fp32 partial maxima (|x| as uint32 bits, so
+ * unsigned max == float max, and NaN sorts above +Inf).  Because the
+ * partials are plain maxima, an element-wise integer MAX all-reduce of the
+ * buffer across ranks yields the global absmax (config 5). */
+#define KZ_PARTIALS_WORDS 1024
+
+/* ------------------------------------------------------------------ misc */
+
+const char* kz_last_error(void);
+int kz_version(void);
+/* 1 when `device` is an sm_100 GPU this library has code for, else 0. */
+int kz_device_supported(int device);
+
+/* Replaces Tensor::randn (core/src/Tensor.cpp:85-92): fills n floats on the
+ * HOST from std::mt19937(seed) through std::normal_distribution<float>(0, std),
+ * the same generator and distribution the reference uses, so weights created
+ * with a seed equal the reference's bit for bit.  seed == 0 draws a random seed
+ * as the reference does. */
+int kz_randn_host(float* out, int64_t n, float stddev, uint64_t seed);
+
+/* Reads the current device's sticky status word (0 or a kz_status_code) after
+ * synchronising `stream`; clears it when `clear` != 0. */
+int kz_device_status(int* code, int clear, kz_stream_t stream);
+
+/* ------------------------------------------- quantize (quantize.py:50-70) */
+
+/* Per-tensor absmax of x[0..n): writes partial maxima into `partials`.
+ * Replaces `max(abs(v) for v in flat)` (quantize.py:67). */
+int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t stream);
+
+/* Per-tensor quantize given absmax partials (from kz_absmax_f32, the int8
+ * GEMM's epilogue, or a MAX all-reduce of either across ranks).
+ * Replaces quantize.py:68-69: scale = max_abs / 127 (double; 1.0 when
+ * max_abs == 0), q = clamp(round_half_even(x / scale), -127, 127), bit-exact.
+ * Writes q[0..n), *scale (double) and *scale_f32 ((float)*scale, may be NULL).
+ * A NaN/Inf absmax writes q = 0, *scale = NaN and sets KZ_ERR_NONFINITE in
+ * the device status word. */
+int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials, int8_t* q,
+                             double* scale, float* scale_f32, kz_stream_t stream);
+
+/* quantize_symmetric (quantize.py:50-70) on the device: kz_absmax_f32 then
+ * kz_quantize_partials_f32; `partials` is caller scratch. */
+int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
+                           uint32_t* partials, kz_stream_t stream);
+
+/* Per-output-channel quantize of a reference-layout weight w[K, N] (row-major,
+ * nn.py:74-81: [in_features, out_features]); channel n is column n.  Writes
+ * K-major codes qT[N, K], scales[N] (double) and scales_f32[N].  Each column
+ * follows quantize.py:66-70 exactly.  `workspace` must hold
+ * kz_quantize_cols_workspace_bytes(K, N) bytes. */
+size_t kz_quantize_cols_workspace_bytes(int64_t K, int64_t N);
+int kz_quantize_cols_f32(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales, float* scales_f32,
+                         void* workspace, size_t workspace_bytes, kz_stream_t stream);
+
+/* Per-row (per-token) quantize of x[M, K]: row m gets its own scale,
+ * quantize.py:66-70 applied to each row. */
+int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double* scales, float* scales_f32,
+                         kz_stream_t stream);
+
+/* ----------------------------------------- dequantize (quantize.py:73-77) */
+
+/* out[i] = (float)((double)q[i] * scale): quantize.py:76 in double, narrowed
+ * to fp32 as Tensor::from_flat does (core/src/Tensor.cpp:94-100). */
+int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, kz_stream_t stream);
+
+/* Inverse of kz_quantize_cols_f32: out[K, N] (reference layout) from qT[N, K]
+ * and per-channel double scales (device pointer). */
+int kz_dequantize_cols_i8_f32(const int8_t* qT, int64_t K, int64_t N, const double* scales, float* out,
+                              kz_stream_t stream);
+
+/* ------------------------------- qlinear, reference semantics (W8A32) */
+
+/* Replaces qlinear (quantize.py:115-122) = Tensor::matmul (core/src/Tensor.cpp:332-362
+ * -> backend/cpu/src/Ops.cpp:328-337) on dequantize(q, scale), then
+ * Tensor::add bias (Ops.cpp:34-38), then an optional activation (nn.ReLU ->
+ * Ops.cpp:197-199, nn.GELU -> Ops.cpp:250-256).
+ * out[M, N] = act(x[M, K] @ dequantize(q[K, N], scale) + bias[N]); bias may be NULL.
+ * Accumulation runs in k order with every product and sum rounded to fp32
+ * separately, as the reference's loop does, so relu/none outputs are
+ * bit-identical to the reference. */
+int kz_qlinear_w8a32_f32(const float* x, int64_t M, int64_t K, const int8_t* q, double scale,
+                         const float* bias, int64_t N, int act, float* out, kz_stream_t stream);
+
+/* ------------------------------------------------- int8 GEMM (W8A8) */
+
+/* acc[m, n] = sum_k A[m, k] * B[n, k]  (int8 x int8 -> int32, exact), on the
+ * sm_100a tensor cores (tcgen05.mma kind::i8, TMA-fed, TMEM accumulators).
+ * New behaviour: the reference has no int8 GEMM (quantize.py:35-44); this is
+ * the contraction inside qlinear (quantize.py:121) once both operands are int8.
+ *
+ *   A: int8, K-major.  With a_kblock == K it is the plain row-major [M, K].
+ *      With a_kblock = K / G it is G blocks [G][M][K/G] (block g holds columns
+ *      g*K/G .. of A): the rank-major layout an all-gather of G column shards
+ *      produces, consumed without relayout.  a_kblock must divide K and, when
+ *      != K, be a multiple of 128.
+ *   B: int8 [N, K], K-major (the weight codes kz_quantize_cols_f32 writes).
+ *   K must be a multiple of 16 (TMA row pitch); M, N, K > 0 otherwise ragged.
+ *
+ * Epilogue, fused (each step an fp32 operation, round to nearest):
+ *   y = ((float)acc * row_scale[m * rs_stride]) * col_scale[n * cs_stride]
+ *   y = y + bias[n]            (bias may be NULL)
+ *   y = act(y)
+ * rs_stride / cs_stride: 0 broadcasts one scale (per-tensor), 1 indexes it
+ * (per-row / per-channel).  Scales may be NULL only when out_f32 is NULL.
+ * Outputs (either may be NULL, not both): out_f32[M, ldo] = y and
+ * out_i32[M, ldo] = acc.
+ * absmax_partials (may be NULL): receives partial maxima of |y| in the
+ * KZ_PARTIALS_WORDS format, so the output can be re-quantized per tensor by
+ * kz_quantize_partials_f32 without another pass over it. */
+int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
+               const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
+               const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
+               uint32_t* absmax_partials, kz_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KZ_H_ */

@@ -1,0 +1,483 @@
+// Scale finding, quantize and dequantize for Kansai's int8 path
+// (python/kansai/quantize.py:50-77), as HBM-bound sm_100a kernels.
+//
+// Rounding contract (bit-exact with the reference): every fp32 element is
+// widened to double, scale = (double)max|x| / 127.0 (1.0 if max|x| == 0),
+// q = clamp(rint((double)x / scale), -127, 127) with rint rounding half to
+// even on the correctly rounded double quotient.
+//
+// Fast path.  The exact double division per element is replaced by an fp32
+// estimate t = fl32(x * r), r = fl32(fl64(1 / scale)).  With |x / scale| <= 127:
+//   |r - 1/scale| <= (2^-53 + 2^-24 + 2^-77) / scale
+//   |t - x*r|     <= 2^-24 |x*r|   (+2^-149 if t is subnormal)
+// so |t - x/scale| < 127 * 2^-22.9 < 2^-16, and the double quotient differs
+// from x/scale by at most 128 * 2^-53.  Hence |t - fl64(x/scale)| < 2^-15.
+// Whenever t lies at least 2^-12 away from every half-integer
+// (|t - rint(t)| <= 1/2 - 2^-12), fl64(x/scale) lies in the same open interval
+// (k - 1/2, k + 1/2) and rounds to the same k = rint(t).  The remaining
+// elements (about 1 in 2000 for smooth data) take the exact double division.
+// t - rint(t) is computed exactly (Sterbenz).  When 1/scale does not fit fp32
+// (max|x| < 2^-100) every element takes the exact path.
+#include <cfloat>
+
+#include "kz_common.cuh"
+
+namespace kz {
+
+constexpr float kTieGuard = 0.5f - 1.0f / 4096.0f;
+constexpr uint32_t kInfBits = 0x7F800000u;
+
+__device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+
+// ---------------------------------------------------------------- absmax
+
+// Grid-stride max of |x| bits; block b writes partials[1 + b], block 0 writes
+// the count.  NaN bit patterns exceed +Inf's, so they survive the max.
+__global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ x, int64_t n,
+                                                     uint32_t* __restrict__ partials) {
+    uint32_t m = 0;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+    if (aligned) {
+        const int64_t nv = n >> 2;
+        const float4* xv = reinterpret_cast<const float4*>(x);
+        int64_t i = tid;
+        // four independent 16-byte loads in flight per thread
+        for (; i + 3 * nthreads < nv; i += 4 * nthreads) {
+            float4 a = __ldcs(xv + i);
+            float4 b = __ldcs(xv + i + nthreads);
+            float4 c = __ldcs(xv + i + 2 * nthreads);
+            float4 d = __ldcs(xv + i + 3 * nthreads);
+            m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
+            m = max(m, max(max(abs_bits(b.x), abs_bits(b.y)), max(abs_bits(b.z), abs_bits(b.w))));
+            m = max(m, max(max(abs_bits(c.x), abs_bits(c.y)), max(abs_bits(c.z), abs_bits(c.w))));
+            m = max(m, max(max(abs_bits(d.x), abs_bits(d.y)), max(abs_bits(d.z), abs_bits(d.w))));
+        }
+        for (; i < nv; i += nthreads) {
+            float4 a = __ldcs(xv + i);
+            m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
+        }
+        for (int64_t j = (nv << 2) + tid; j < n; j += nthreads) m = max(m, abs_bits(x[j]));
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) m = max(m, abs_bits(x[j]));
+    }
+    m = warp_max_u32(m);
+    __shared__ uint32_t red[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) {
+            partials[1 + blockIdx.x] = v;
+            if (blockIdx.x == 0) partials[0] = gridDim.x;
+        }
+    }
+}
+
+// ------------------------------------------------------- scale + quantize
+
+struct ScaleInfo {
+    double scale;   // the reference's double scale
+    float rcp;      // fl32(fl64(1 / scale)), fast-path multiplier
+    bool fast;      // fast path valid (1/scale representable in fp32)
+    bool finite;    // absmax finite
+};
+
+__device__ __forceinline__ ScaleInfo scale_from_absmax_bits(uint32_t bits) {
+    ScaleInfo si;
+    si.finite = bits < kInfBits;
+    const float a = __uint_as_float(bits);
+    si.scale = a > 0.0f ? (double)a / 127.0 : 1.0;   // quantize.py:68
+    si.rcp = __double2float_rn(1.0 / si.scale);
+    si.fast = a >= 7.8886090522101181e-31f;           // 2^-100
+    return si;
+}
+
+__device__ __forceinline__ int8_t quant_exact(float v, double scale) {
+    double t = rint((double)v / scale);               // quantize.py:69, IEEE division
+    t = fmin(fmax(t, -127.0), 127.0);
+    return (int8_t)(int)t;
+}
+
+__device__ __forceinline__ int8_t quant_one(float v, const ScaleInfo& si) {
+    if (si.fast) {
+        const float t = __fmul_rn(v, si.rcp);
+        const float tr = rintf(t);
+        if (fabsf(t - tr) <= kTieGuard) return (int8_t)(int)fminf(fmaxf(tr, -127.0f), 127.0f);
+    }
+    return quant_exact(v, si.scale);
+}
+
+__device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) {
+    uint32_t b0 = (uint8_t)quant_one(v.x, si), b1 = (uint8_t)quant_one(v.y, si);
+    uint32_t b2 = (uint8_t)quant_one(v.z, si), b3 = (uint8_t)quant_one(v.w, si);
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// Reduce a partials buffer inside one block; every thread gets the result.
+__device__ __forceinline__ uint32_t block_reduce_partials(const uint32_t* __restrict__ partials) {
+    __shared__ uint32_t red[32];
+    __shared__ uint32_t result;
+    const uint32_t count = min(partials[0], (uint32_t)(KZ_PARTIALS_WORDS - 1));
+    uint32_t m = 0;
+    for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) m = max(m, partials[1 + i]);
+    m = warp_max_u32(m);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) result = v;
+    }
+    __syncthreads();
+    return result;
+}
+
+__global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __restrict__ x, int64_t n,
+                                                                const uint32_t* __restrict__ partials,
+                                                                int8_t* __restrict__ q, double* scale_out,
+                                                                float* scale_f32_out, int* status) {
+    const uint32_t bits = block_reduce_partials(partials);
+    const ScaleInfo si = scale_from_absmax_bits(bits);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (si.finite) {
+            *scale_out = si.scale;
+            if (scale_f32_out) *scale_f32_out = __double2float_rn(si.scale);
+        } else {
+            *scale_out = __longlong_as_double(0x7FF8000000000000ll);
+            if (scale_f32_out) *scale_f32_out = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+    if (!si.finite) {
+        for (int64_t j = tid; j < n; j += nthreads) q[j] = 0;
+        return;
+    }
+    if (aligned) {
+        // 16 elements per thread per step: 64 B in, one 16 B store out.
+        const int64_t n16 = n >> 4;
+        const float4* xv = reinterpret_cast<const float4*>(x);
+        uint4* qv = reinterpret_cast<uint4*>(q);
+        for (int64_t i = tid; i < n16; i += nthreads) {
+            const float4 a = __ldcs(xv + 4 * i), b = __ldcs(xv + 4 * i + 1);
+            const float4 c = __ldcs(xv + 4 * i + 2), d = __ldcs(xv + 4 * i + 3);
+            uint4 o;
+            o.x = pack4(a, si);
+            o.y = pack4(b, si);
+            o.z = pack4(c, si);
+            o.w = pack4(d, si);
+            __stcs(qv + i, o);
+        }
+        for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
+    }
+}
+
+// ------------------------------------------------------ per-column (weights)
+
+// Column absmax partials: partial[r][n] = max over rows of split r of |w[k][n]|.
+// Block (32, 8): threadIdx.x walks 32 adjacent columns (128 B coalesced rows),
+// threadIdx.y strides rows.
+__global__ void __launch_bounds__(256) absmax_cols_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                                          int64_t rows_per_split, uint32_t* __restrict__ partial) {
+    const int64_t n = blockIdx.x * 32 + threadIdx.x;
+    const int64_t k0 = blockIdx.y * rows_per_split;
+    const int64_t k1 = min(K, k0 + rows_per_split);
+    uint32_t m = 0;
+    if (n < N)
+        for (int64_t k = k0 + threadIdx.y; k < k1; k += 8) m = max(m, abs_bits(__ldg(w + k * N + n)));
+    __shared__ uint32_t red[8][33];
+    red[threadIdx.y][threadIdx.x] = m;
+    __syncthreads();
+    if (threadIdx.y == 0 && n < N) {
+#pragma unroll
+        for (int i = 1; i < 8; ++i) m = max(m, red[i][threadIdx.x]);
+        partial[blockIdx.y * N + n] = m;
+    }
+}
+
+// Transposing quantize: tile of 128 rows (k) x 32 columns (n) of w[K, N] ->
+// qT[n][k0 .. k0 + 128).  Thread x owns column n0 + x for the whole tile, so it
+// derives that column's scale once from the split partials.
+__global__ void __launch_bounds__(256) quantize_cols_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                                            const uint32_t* __restrict__ partial, int splits,
+                                                            int8_t* __restrict__ qT, double* scales,
+                                                            float* scales_f32, int* status) {
+    __shared__ __align__(16) int8_t tile[32][128 + 16];
+    const int64_t n0 = blockIdx.x * 32;
+    const int64_t k0 = blockIdx.y * 128;
+    const int64_t n = n0 + threadIdx.x;
+    uint32_t bits = 0;
+    if (n < N)
+        for (int r = 0; r < splits; ++r) bits = max(bits, partial[r * N + n]);
+    const ScaleInfo si = scale_from_absmax_bits(bits);
+    if (blockIdx.y == 0 && threadIdx.y == 0 && n < N) {
+        if (si.finite) {
+            scales[n] = si.scale;
+            if (scales_f32) scales_f32[n] = __double2float_rn(si.scale);
+        } else {
+            scales[n] = __longlong_as_double(0x7FF8000000000000ll);
+            if (scales_f32) scales_f32[n] = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    for (int kk = threadIdx.y; kk < 128; kk += 8) {
+        const int64_t k = k0 + kk;
+        int8_t v = 0;
+        if (n < N && k < K && si.finite) v = quant_one(__ldg(w + k * N + n), si);
+        tile[threadIdx.x][kk] = v;
+    }
+    __syncthreads();
+    // write out: 32 rows of qT x 128 bytes; thread t -> row t / 8, 16-byte chunk t % 8
+    const int t = threadIdx.y * 32 + threadIdx.x;
+    const int row = t >> 3, chunk = t & 7;
+    const int64_t nn = n0 + row;
+    const int64_t kb = k0 + chunk * 16;
+    if (nn < N && kb < K) {
+        int8_t* dst = qT + nn * K + kb;
+        if (kb + 16 <= K && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[row][chunk * 16]);
+        } else {
+            for (int j = 0; j < 16 && kb + j < K; ++j) dst[j] = tile[row][chunk * 16 + j];
+        }
+    }
+}
+
+// --------------------------------------------------------- per-row (tokens)
+
+// One block per row: absmax then quantize of that row.
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int64_t M, int64_t K,
+                                                            int8_t* __restrict__ q, double* scales,
+                                                            float* scales_f32, int* status) {
+    const int64_t row = blockIdx.x;
+    const float* xr = x + row * K;
+    int8_t* qr = q + row * K;
+    uint32_t m = 0;
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) m = max(m, abs_bits(xr[j]));
+    m = warp_max_u32(m);
+    __shared__ uint32_t red[32];
+    __shared__ uint32_t res;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) res = v;
+    }
+    __syncthreads();
+    const ScaleInfo si = scale_from_absmax_bits(res);
+    if (threadIdx.x == 0) {
+        if (si.finite) {
+            scales[row] = si.scale;
+            if (scales_f32) scales_f32[row] = __double2float_rn(si.scale);
+        } else {
+            scales[row] = __longlong_as_double(0x7FF8000000000000ll);
+            if (scales_f32) scales_f32[row] = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) qr[j] = si.finite ? quant_one(xr[j], si) : (int8_t)0;
+}
+
+// -------------------------------------------------------------- dequantize
+
+// Per-tensor dequantize through a 255-entry table: table[q + 127] =
+// (float)((double)q * scale) holds every value the reference can produce, so
+// the per-element work is one shared-memory lookup (1 B in, 4 B out).
+__global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restrict__ q, int64_t n, double scale,
+                                                         float* __restrict__ out) {
+    __shared__ float table[256];
+    if (threadIdx.x < 255) table[threadIdx.x] = __double2float_rn((double)((int)threadIdx.x - 127) * scale);
+    if (threadIdx.x == 255) table[255] = __double2float_rn(-128.0 * scale);
+    __syncthreads();
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    auto lut = [&](uint32_t byte) { return table[(((int)(int8_t)(uint8_t)byte) + 127) & 255]; };
+    const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+    if (aligned) {
+        const int64_t n16 = n >> 4;
+        const uint4* qv = reinterpret_cast<const uint4*>(q);
+        float4* ov = reinterpret_cast<float4*>(out);
+        for (int64_t i = tid; i < n16; i += nthreads) {
+            const uint4 c = __ldcs(qv + i);
+            const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float4 o;
+                o.x = lut(w[j] & 0xFF);
+                o.y = lut((w[j] >> 8) & 0xFF);
+                o.z = lut((w[j] >> 16) & 0xFF);
+                o.w = lut(w[j] >> 24);
+                __stcs(ov + 4 * i + j, o);
+            }
+        }
+        for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
+    }
+}
+
+// out[k][n] = (float)((double)qT[n][k] * scales[n]); 32x32 tiles through smem.
+__global__ void __launch_bounds__(256) dequantize_cols_kernel(const int8_t* __restrict__ qT, int64_t K, int64_t N,
+                                                              const double* __restrict__ scales,
+                                                              float* __restrict__ out) {
+    __shared__ int8_t tile[32][33];
+    const int64_t n0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int64_t n = n0 + r, k = k0 + threadIdx.x;
+        tile[r][threadIdx.x] = (n < N && k < K) ? qT[n * K + k] : (int8_t)0;
+    }
+    __syncthreads();
+    const int64_t n = n0 + threadIdx.x;
+    const double s = n < N ? scales[n] : 0.0;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int64_t k = k0 + r;
+        if (n < N && k < K) out[k * N + n] = __double2float_rn((double)tile[threadIdx.x][r] * s);
+    }
+}
+
+static int elementwise_grid(int64_t work_items) {
+    const int64_t cap = (int64_t)sm_count() * 8;   // 8 resident 256-thread blocks per SM
+    int64_t g = (work_items + 255) / 256;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return (int)g;
+}
+
+}  // namespace kz
+
+using namespace kz;
+
+extern "C" {
+
+int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t stream) {
+    KZ_REQUIRE(n >= 0, "kz_absmax_f32: n must be >= 0");
+    KZ_REQUIRE(partials != nullptr, "kz_absmax_f32: partials is NULL");
+    KZ_REQUIRE(n == 0 || x != nullptr, "kz_absmax_f32: x is NULL");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int grid = elementwise_grid((n + 15) / 16);
+    if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
+    if (grid > 4 * sm_count()) grid = 4 * sm_count();
+    absmax_kernel<<<grid, 256, 0, s>>>(x, n, partials);
+    return launch_status("absmax_kernel");
+}
+
+int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials, int8_t* q, double* scale,
+                             float* scale_f32, kz_stream_t stream) {
+    KZ_REQUIRE(n >= 0, "kz_quantize_partials_f32: n must be >= 0");
+    KZ_REQUIRE(partials && scale, "kz_quantize_partials_f32: partials and scale must be non-NULL");
+    KZ_REQUIRE(n == 0 || (x && q), "kz_quantize_partials_f32: x or q is NULL");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    quantize_partials_kernel<<<elementwise_grid((n + 15) / 16), 256, 0, s>>>(x, n, partials, q, scale, scale_f32,
+                                                                              device_status_ptr());
+    return launch_status("quantize_partials_kernel");
+}
+
+int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
+                           uint32_t* partials, kz_stream_t stream) {
+    int st = kz_absmax_f32(x, n, partials, stream);
+    if (st) return st;
+    return kz_quantize_partials_f32(x, n, partials, q, scale, scale_f32, stream);
+}
+
+static int64_t col_splits(int64_t K, int64_t N) {
+    // enough blocks to fill the GPU: ~4 waves of (N / 32) x splits
+    const int64_t col_tiles = (N + 31) / 32;
+    int64_t want = (4 * (int64_t)sm_count() + col_tiles - 1) / col_tiles;
+    int64_t max_splits = (K + 63) / 64;   // at least 64 rows per split
+    if (want > max_splits) want = max_splits;
+    if (want < 1) want = 1;
+    if (want > 64) want = 64;
+    return want;
+}
+
+size_t kz_quantize_cols_workspace_bytes(int64_t K, int64_t N) {
+    if (K <= 0 || N <= 0) return 0;
+    return (size_t)64 * (size_t)N * sizeof(uint32_t);
+}
+
+int kz_quantize_cols_f32(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales, float* scales_f32,
+                         void* workspace, size_t workspace_bytes, kz_stream_t stream) {
+    KZ_REQUIRE(K >= 0 && N >= 0, "kz_quantize_cols_f32: K and N must be >= 0");
+    if (K == 0 || N == 0) {
+        KZ_REQUIRE(N == 0 || scales, "kz_quantize_cols_f32: scales is NULL");
+        if (N == 0) return KZ_OK;
+    }
+    KZ_REQUIRE(scales != nullptr, "kz_quantize_cols_f32: scales is NULL");
+    KZ_REQUIRE(K == 0 || (w && qT), "kz_quantize_cols_f32: w or qT is NULL");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t splits = K == 0 ? 1 : col_splits(K, N);
+    KZ_REQUIRE(workspace != nullptr && workspace_bytes >= (size_t)splits * (size_t)N * sizeof(uint32_t),
+               "kz_quantize_cols_f32: workspace smaller than kz_quantize_cols_workspace_bytes(K, N)");
+    uint32_t* partial = static_cast<uint32_t*>(workspace);
+    if (K == 0) {
+        KZ_CHECK_CUDA(cudaMemsetAsync(partial, 0, (size_t)N * sizeof(uint32_t), s));
+    } else {
+        const int64_t rows_per_split = (K + splits - 1) / splits;
+        absmax_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)splits), dim3(32, 8), 0, s>>>(
+            w, K, N, rows_per_split, partial);
+        st = launch_status("absmax_cols_kernel");
+        if (st) return st;
+    }
+    const int64_t ktiles = K == 0 ? 1 : (K + 127) / 128;
+    KZ_REQUIRE(ktiles < 65536, "kz_quantize_cols_f32: K too large");
+    quantize_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)ktiles), dim3(32, 8), 0, s>>>(
+        w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
+    return launch_status("quantize_cols_kernel");
+}
+
+int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double* scales, float* scales_f32,
+                         kz_stream_t stream) {
+    KZ_REQUIRE(M >= 0 && K >= 0, "kz_quantize_rows_f32: M and K must be >= 0");
+    if (M == 0) return KZ_OK;
+    KZ_REQUIRE(scales != nullptr, "kz_quantize_rows_f32: scales is NULL");
+    KZ_REQUIRE(K == 0 || (x && q), "kz_quantize_rows_f32: x or q is NULL");
+    KZ_REQUIRE(M < (int64_t)INT32_MAX, "kz_quantize_rows_f32: M too large");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    quantize_rows_kernel<<<(unsigned)M, 256, 0, s>>>(x, M, K, q, scales, scales_f32, device_status_ptr());
+    return launch_status("quantize_rows_kernel");
+}
+
+int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, kz_stream_t stream) {
+    KZ_REQUIRE(n >= 0, "kz_dequantize_i8_f32: n must be >= 0");
+    if (n == 0) return KZ_OK;
+    KZ_REQUIRE(q && out, "kz_dequantize_i8_f32: q or out is NULL");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    dequantize_kernel<<<elementwise_grid((n + 15) / 16), 256, 0, s>>>(q, n, scale, out);
+    return launch_status("dequantize_kernel");
+}
+
+int kz_dequantize_cols_i8_f32(const int8_t* qT, int64_t K, int64_t N, const double* scales, float* out,
+                              kz_stream_t stream) {
+    KZ_REQUIRE(K >= 0 && N >= 0, "kz_dequantize_cols_i8_f32: K and N must be >= 0");
+    if (K == 0 || N == 0) return KZ_OK;
+    KZ_REQUIRE(qT && scales && out, "kz_dequantize_cols_i8_f32: NULL pointer");
+    KZ_REQUIRE((N + 31) / 32 < 65536, "kz_dequantize_cols_i8_f32: N too large");
+    int st = check_device();
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    dequantize_cols_kernel<<<dim3((unsigned)((K + 31) / 32), (unsigned)((N + 31) / 32)), dim3(32, 8), 0, s>>>(
+        qT, K, N, scales, out);
+    return launch_status("dequantize_cols_kernel");
+}
+
+}  // extern "C"

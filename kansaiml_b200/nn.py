@@ -1,0 +1,204 @@
+"""Model hosts for the quantized path, with the reference's nn names (python/kansai/nn.py).
+
+Only the layers the int8 configurations need: Linear (nn.py:74-81, weight
+[in, out] with std 1/sqrt(in) from the reference's own randn stream, zero
+bias), ReLU / GELU (nn.py:216-218 and the exact-erf GELU), Sequential
+(nn.py:649-656), and the transformer pieces of config 3 (LayerNorm nn.py:308-331,
+MultiHeadAttention nn.py:334-427, TransformerBlock nn.py:430-478, Embedding
+nn.py:624-646).  Inference only: no autograd.
+
+Sequential fuses ``QLinear`` followed by ``ReLU`` / ``GELU`` into the
+quantized kernel's epilogue; the activation is applied to the same fp32 value,
+so the result equals running the two layers one after the other.
+"""
+import math
+
+import torch
+
+from .quantize import QLinear
+from .tensor import Tensor, as_tensor, from_flat, ones, randn, zeros
+
+
+class Module:
+    training = False
+
+    def __call__(self, *args, **kwargs):
+        return self.forward(*args, **kwargs)
+
+    def forward(self, *args, **kwargs):
+        raise NotImplementedError
+
+    def named_parameters(self, prefix=""):
+        for name, value in vars(self).items():
+            full = f"{prefix}{name}"
+            if isinstance(value, Tensor):
+                yield full, value
+            elif isinstance(value, Module):
+                yield from value.named_parameters(full + ".")
+            elif isinstance(value, (list, tuple)):
+                for i, item in enumerate(value):
+                    if isinstance(item, Module):
+                        yield from item.named_parameters(f"{full}.{i}.")
+
+    def parameters(self):
+        return [t for _, t in self.named_parameters()]
+
+    def eval(self):
+        return self
+
+
+class Linear(Module):
+    """nn.py:74-81: weight [in, out] ~ N(0, 1/in) from randn(seed), bias zeros."""
+
+    def __init__(self, in_features, out_features, seed=0, device=None):
+        std = 1.0 / math.sqrt(in_features)
+        self.weight = randn([in_features, out_features], std=std, seed=seed, device=device)
+        self.bias = zeros([out_features], device=device)
+
+    def forward(self, x):
+        return as_tensor(x).matmul(self.weight).add(self.bias)
+
+
+class ReLU(Module):
+    def forward(self, x):
+        return as_tensor(x).relu()
+
+
+class GELU(Module):
+    def forward(self, x):
+        return as_tensor(x).gelu()
+
+
+_FUSABLE = {ReLU: "relu", GELU: "gelu"}
+
+
+class Sequential(Module):
+    def __init__(self, *layers):
+        self.layers = list(layers)
+
+    def forward(self, x):
+        i, n = 0, len(self.layers)
+        while i < n:
+            layer = self.layers[i]
+            nxt = self.layers[i + 1] if i + 1 < n else None
+            if isinstance(layer, QLinear) and type(nxt) in _FUSABLE:
+                x = layer(x, act=_FUSABLE[type(nxt)])
+                i += 2
+                continue
+            x = layer(x)
+            i += 1
+        return x
+
+
+class LayerNorm(Module):
+    """nn.py:308-331: normalises the last axis, biased variance, eps 1e-5."""
+
+    def __init__(self, num_features, eps=1e-5, device=None):
+        self.num_features = num_features
+        self.eps = eps
+        self.weight = ones([num_features], device=device)
+        self.bias = zeros([num_features], device=device)
+
+    def forward(self, x):
+        t = as_tensor(x).data
+        mean = t.mean(-1, keepdim=True)
+        centered = t - mean
+        var = (centered * centered).mean(-1, keepdim=True)
+        normed = centered / torch.sqrt(var + self.eps)
+        return Tensor(normed * self.weight.data + self.bias.data)
+
+
+class Embedding(Module):
+    """nn.py:624-646: weight [vocab, dim] ~ N(0, 1) from randn(seed); forward
+    takes (nested) integer ids."""
+
+    def __init__(self, num_embeddings, embedding_dim, seed=0, device=None):
+        self.weight = randn([num_embeddings, embedding_dim], std=1.0, seed=seed, device=device)
+
+    def forward(self, ids):
+        idx = ids if isinstance(ids, torch.Tensor) else torch.as_tensor(ids, dtype=torch.long)
+        idx = idx.to(self.weight.data.device)
+        return Tensor(self.weight.data[idx])
+
+
+class MultiHeadAttention(Module):
+    """nn.py:334-427: raw [d, d] projections w_q, w_k, w_v, w_o (no bias),
+    scaled dot-product attention with an optional additive mask, fp32.
+    ``quantize(per_channel=True)`` swaps the four projections for int8 QLinear
+    layers (bias-free); attention scores and softmax stay fp32."""
+
+    def __init__(self, d_model, num_heads, seed=0, device=None):
+        if d_model % num_heads:
+            raise ValueError(f"MultiHeadAttention: d_model={d_model} must be divisible by num_heads={num_heads}")
+        self.d_model, self.num_heads, self.d_k = d_model, num_heads, d_model // num_heads
+        std = 1.0 / math.sqrt(d_model)
+        self.w_q = randn([d_model, d_model], std=std, seed=seed, device=device)
+        self.w_k = randn([d_model, d_model], std=std, seed=seed + 1, device=device)
+        self.w_v = randn([d_model, d_model], std=std, seed=seed + 2, device=device)
+        self.w_o = randn([d_model, d_model], std=std, seed=seed + 3, device=device)
+        self.q_proj = None
+
+    def quantize(self, per_channel=True, activations=None):
+        class _W:  # a Linear-shaped view of a bias-free projection
+            def __init__(self, w):
+                self.weight, self.bias = w, None
+        self.q_proj = [QLinear(_W(w), per_channel=per_channel, activations=activations)
+                       for w in (self.w_q, self.w_k, self.w_v, self.w_o)]
+        return self
+
+    def _proj(self, x, i, w):
+        if self.q_proj is not None:
+            return self.q_proj[i](x)
+        return x.matmul(w)
+
+    def forward(self, query, key, value, mask=None):
+        q_in, k_in, v_in = as_tensor(query), as_tensor(key), as_tensor(value)
+        b, sq, _ = q_in.shape
+        _, sk, _ = k_in.shape
+        h, dk = self.num_heads, self.d_k
+        q = self._proj(q_in, 0, self.w_q).data.reshape(b, sq, h, dk).transpose(1, 2)
+        k = self._proj(k_in, 1, self.w_k).data.reshape(b, sk, h, dk).transpose(1, 2)
+        v = self._proj(v_in, 2, self.w_v).data.reshape(b, sk, h, dk).transpose(1, 2)
+        scores = torch.matmul(q, k.transpose(2, 3)) * (1.0 / math.sqrt(dk))
+        if mask is not None:
+            scores = scores + as_tensor(mask).data
+        att = torch.matmul(torch.softmax(scores, 3), v)
+        merged = Tensor(att.transpose(1, 2).reshape(b, sq, self.d_model).contiguous())
+        return self._proj(merged, 3, self.w_o)
+
+
+class TransformerBlock(Module):
+    """nn.py:430-478: pre-LN attention and GELU feed-forward, both residual."""
+
+    def __init__(self, d_model, num_heads, d_ff, seed=0, device=None):
+        self.ln1 = LayerNorm(d_model, device=device)
+        self.attn = MultiHeadAttention(d_model, num_heads, seed=seed, device=device)
+        self.ln2 = LayerNorm(d_model, device=device)
+        self.fc1 = Linear(d_model, d_ff, seed=seed + 100, device=device)
+        self.gelu = GELU()
+        self.fc2 = Linear(d_ff, d_model, seed=seed + 101, device=device)
+
+    def quantize(self, per_channel=True, activations=None):
+        """Every Linear weight to int8 (fc1, fc2 and the four attention projections)."""
+        self.attn.quantize(per_channel, activations)
+        self.fc1 = QLinear(self.fc1, per_channel=per_channel, activations=activations)
+        self.fc2 = QLinear(self.fc2, per_channel=per_channel, activations=activations)
+        return self
+
+    def forward(self, x, mask=None):
+        x = as_tensor(x)
+        normed = self.ln1(x)
+        x = x.add(self.attn(normed, normed, normed, mask=mask))
+        h = self.ln2(x)
+        if isinstance(self.fc1, QLinear):
+            h = self.fc1(h, act="gelu")
+        else:
+            h = self.gelu(self.fc1(h))
+        return x.add(self.fc2(h))
+
+
+def causal_mask(seq, device=None):
+    """Additive causal mask [1, 1, seq, seq] (0 allowed, -1e9 masked), the
+    convention of examples/tinyshakespeare/train_shakespeare.py:96-97."""
+    vals = torch.full((seq, seq), -1e9, dtype=torch.float32).triu(1)
+    return from_flat(vals.reshape(-1).tolist(), [1, 1, seq, seq], device=device)

@@ -26,7 +26,7 @@ def load_reference_core():
     name = next((f for f in os.listdir(REF_BUILD) if f.startswith("_core") and f.endswith(".so")), None)
     if name is None:
         raise ImportError("oracle/_ref has no compiled reference core; run `make -C oracle ref`")
-    spec = importlib.util.spec_from_file_location("kz_reference_core", os.path.join(REF_BUILD, name))
+    spec = importlib.util.spec_from_file_location("_core", os.path.join(REF_BUILD, name))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod

@@ -1,0 +1,75 @@
+"""CPU checks of the drop-in boundary: libkz.so loads without a GPU, exports
+every entry point include/kz.h declares (and the ctypes table binds each one),
+and its host-only pieces behave as specified.  No kernel is launched here."""
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+from kansaiml_b200 import _lib
+
+
+def declared_symbols():
+    text = open(_lib.INCLUDE_H).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kz_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in include/kz.h but not exported"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes table and include/kz.h disagree"
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.kz_version() >= 1
+    assert isinstance(_lib.last_error(), str)
+
+
+def test_randn_matches_reference_stream():
+    """kz_randn_host reproduces Tensor::randn (std::mt19937 + normal_distribution):
+    the reference Linear(784, 256, seed=1) weight hash is in the golden fixture."""
+    import inputs
+    from conftest import golden
+    from kansaiml_b200.tensor import randn_host
+    g = golden("mlp_config1.npz")
+    w1 = randn_host([784, 256], std=1.0 / 28.0, seed=1)
+    assert inputs.sha(w1) == str(g["w1_sha256"])
+    np.testing.assert_array_equal(w1[0], g["w1_first_row"])
+
+
+def test_host_argument_validation_without_gpu():
+    """Shape checks fail before any device work."""
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    assert lib.kz_gemm_i8(None, None, -1, 1, 16, 16, None, 0, None, 0, None, 0, None, None, 1, None, None) == 1
+    assert "negative" in _lib.last_error()
+    assert lib.kz_gemm_i8(None, None, 4, 4, 16, 16, None, 0, None, 0, None, 0, None, None, 4, None, None) == 1
+    assert "no output" in _lib.last_error()
+    assert lib.kz_gemm_i8(P(16), P(16), 4, 4, 16, 16, None, 0, None, 0, None, 7, None, P(16), 4, None, None) == 1
+    assert "activation" in _lib.last_error()
+    assert lib.kz_gemm_i8(P(16), P(16), 4, 4, 1 << 20, 0, None, 0, None, 0, None, 0, None, P(16), 4, None, None) == 1
+    assert lib.kz_absmax_f32(None, -5, None, None) == 1
+    assert lib.kz_quantize_rows_f32(None, -1, 3, None, None, None, None) == 1
+    assert lib.kz_qlinear_w8a32_f32(None, 1, 1, None, 1.0, None, 1, 9, None, None) == 1
+    # empty work is a successful no-op
+    assert lib.kz_dequantize_i8_f32(None, 0, 1.0, None, None) == 0
+    assert lib.kz_qlinear_w8a32_f32(None, 0, 5, None, 1.0, None, 3, 0, None, None) == 0
+
+
+def test_check_raises_with_message():
+    lib = _lib.load()
+    st = lib.kz_absmax_f32(None, -1, None, None)
+    with pytest.raises(_lib.KzError, match="invalid argument"):
+        _lib.check(st, "kz_absmax_f32")
+
+
+def test_workspace_size_query():
+    lib = _lib.load()
+    assert lib.kz_quantize_cols_workspace_bytes(4096, 4096) >= 4 * 4096
+    assert lib.kz_quantize_cols_workspace_bytes(0, 5) == 0

@@ -1,0 +1,62 @@
+"""Host-side API of kansaiml_b200 on CPU (data movement only, no compute):
+the reference's Tensor surface, factories and error behaviour."""
+import numpy as np
+import pytest
+
+import kansaiml_b200 as kz
+
+
+def test_from_flat_tolist_roundtrip():
+    t = kz.from_flat([1.0, 2.0, 3.0, 4.0, 5.0, 6.0], [2, 3], device="cpu")
+    assert t.shape == [2, 3] and t.numel() == 6
+    assert t.tolist() == [1.0, 2.0, 3.0, 4.0, 5.0, 6.0]
+    with pytest.raises(RuntimeError, match="data length does not match shape"):
+        kz.from_flat([1.0, 2.0], [3], device="cpu")
+
+
+def test_tensor_nested_list():
+    t = kz.tensor([[0, 0], [0, 1], [1, 0], [1, 1]], device="cpu")
+    assert t.shape == [4, 2]
+    assert t.tolist() == [0.0, 0.0, 0.0, 1.0, 1.0, 0.0, 1.0, 1.0]
+
+
+def test_slice_and_cat():
+    vals = np.arange(28, dtype=np.float32)
+    t = kz.from_flat(vals, [7, 4], device="cpu")
+    a, b = t.slice(0, 0, 3), t.slice(0, 3, 7)
+    assert a.shape == [3, 4] and b.shape == [4, 4]
+    assert kz.cat([a, b], 0).tolist() == vals.tolist()
+    with pytest.raises(RuntimeError):
+        t.slice(0, 5, 9)
+
+
+def test_linear_init_matches_reference_hash():
+    import inputs
+    from conftest import golden
+    g = golden("mlp_config1.npz")
+    l1 = kz.nn.Linear(784, 256, seed=1, device="cpu")
+    l2 = kz.nn.Linear(256, 10, seed=2, device="cpu")
+    assert inputs.sha(l1.weight.numpy()) == str(g["w1_sha256"])
+    assert inputs.sha(l2.weight.numpy()) == str(g["w2_sha256"])
+    assert l1.bias.tolist() == [0.0] * 256
+
+
+def test_compute_on_cpu_tensor_fails_loudly():
+    from kansaiml_b200.quantize import QTensor
+    t = kz.from_flat([1.0, 2.0], [2], device="cpu")
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        QTensor.from_tensor(t)
+
+
+def test_qtensor_reference_constructor_and_nbytes():
+    from kansaiml_b200.quantize import QTensor
+    q = QTensor([1, -2, 3, 127], 0.5, [2, 2], device="cpu")
+    assert q.q == [1, -2, 3, 127]
+    assert q.scale == 0.5 and q.shape == [2, 2] and q.nbytes() == 4
+    with pytest.raises(ValueError):
+        QTensor([300], 1.0, [1], device="cpu")
+    pc = QTensor([1, 2, 3, 4, 5, 6], [0.1, 0.2, 0.3], [2, 3], device="cpu")
+    assert pc.granularity == "channel"
+    assert pc.codes.shape == (3, 2)          # stored K-major [N, K]
+    assert pc.q == [1, 2, 3, 4, 5, 6]         # read back in the [K, N] layout
+    assert pc.scale == [0.1, 0.2, 0.3]
