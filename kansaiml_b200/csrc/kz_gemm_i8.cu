@@ -22,6 +22,7 @@
 // bounded waits and frees its TMEM.
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "kz_common.cuh"
@@ -38,8 +39,12 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;        // tile rasterisation: 16 tile-rows per group
+constexpr int EPI_WARPS = 4;
+constexpr int EPI_BUF = 32 * 32 * 4;                 // one warp's 32 x 32 fp32/int32 sub-tile
+constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;       // one staging buffer per warp: 16 KB
 constexpr int NUM_BARS = 2 * STAGES + 2 * NUM_ACC + 1;
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers + slots*/;
+constexpr int COLV_BYTES = EPI_WARPS * 2 * BN * 4;      // per warp: the tile's column scales and bias
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + COLV_BYTES + 256;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 }  // namespace gemm
 
@@ -57,6 +62,7 @@ struct GemmParams {
     float* out_f32;
     int32_t* out_i32;
     int64_t ldo;
+    int tma_out;        // 1: the single output goes through the TMA-store tensor map
     uint32_t* partials;
     int* status;
 };
@@ -71,6 +77,16 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm,
     tn = r / gm;
 }
 
+template <int ACT>
+__device__ __forceinline__ float epi_act_t(float v) {
+    if constexpr (ACT == KZ_ACT_RELU) return v > 0.0f ? v : 0.0f;
+    if constexpr (ACT == KZ_ACT_GELU) {
+        const float cdf = __fmul_rn(0.5f, __fadd_rn(1.0f, erff(__fmul_rn(v, 0.7071067811865476f))));
+        return __fmul_rn(v, cdf);
+    }
+    return v;
+}
+
 __device__ __forceinline__ float epi_act(float v, int act) {
     if (act == KZ_ACT_RELU) return v > 0.0f ? v : 0.0f;
     if (act == KZ_ACT_GELU) {
@@ -80,15 +96,24 @@ __device__ __forceinline__ float epi_act(float v, int act) {
     return v;
 }
 
+// Whole-warp bounded wait: every lane polls, then the warp agrees.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* status, volatile int* abort_flag) {
+    const bool got = mbar_wait(bar, parity, status, abort_flag);
+    return __all_sync(0xffffffffu, got);
+}
+
+template <int ACT>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
     using namespace gemm;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+    uint8_t* sEpi = sB + STAGES * B_STAGE;
+    float* sColv = reinterpret_cast<float*>(sEpi + EPI_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES + COLV_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint32_t* red = tmem_slot + 2;   // 4 words: epilogue absmax per warp
@@ -106,7 +131,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         }
         for (int a = 0; a < NUM_ACC; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 4);   // one arrive per epilogue warp
+            mbar_init(tempty0 + 8 * a, EPI_WARPS);   // one arrive per epilogue warp
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -115,6 +140,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (p.tma_out) tma_prefetch_desc(&tmOut);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -126,24 +152,22 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t armed_mask = 0, armed_phase = 0;   // per stage: armed at least once / parity of last arm
-            bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                int tm, tn;
-                tile_coords(t, p, tm, tn);
-                const int m0 = tm * BM, n0 = tn * BN;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
+        // ------------------------------------------------ TMA producer (whole warp, lane 0 issues)
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t armed_mask = 0, armed_phase = 0;   // per stage: armed at least once / parity of last arm
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+            int tm, tn;
+            tile_coords(t, p, tm, tn);
+            const int m0 = tm * BM, n0 = tn * BN;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!warp_wait(empty0 + 8 * stage, phase ^ 1, p.status, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
                     mbar_arrive_expect_tx(full0 + 8 * stage, STAGE_BYTES);
-                    armed_mask |= 1u << stage;
-                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
                     const int kbyte = kb * BK;
                     int ax = kbyte, ay = m0;
                     if (p.a_kblock != p.K) {
@@ -153,150 +177,211 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                     }
                     tma_load_2d(sA0 + stage * A_STAGE, &tmA, full0 + 8 * stage, ax, ay);
                     tma_load_2d(sB0 + stage * B_STAGE, &tmB, full0 + 8 * stage, kbyte, n0);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
+                }
+                __syncwarp();
+                armed_mask |= 1u << stage;
+                armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
                 }
             }
-            if (!ok) {
-                // unwinding: let every armed copy land before the CTA exits
-                for (int s = 0; s < STAGES; ++s)
-                    if (armed_mask >> s & 1u) mbar_wait(full0 + 8 * s, armed_phase >> s & 1u, nullptr, nullptr);
-            }
         }
+        if (!ok) {
+            // unwinding: let every armed copy land before the CTA exits
+            for (int s = 0; s < STAGES; ++s)
+                if (armed_mask >> s & 1u) mbar_wait(full0 + 8 * s, armed_phase >> s & 1u, nullptr, nullptr);
+        }
+        __syncwarp();
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            bool issued = false;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, p.status, abort_flag)) {
+        // ------------------------------------------------ MMA issuer (whole warp, lane 0 issues)
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        bool issued = false;
+        for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+            if (!warp_wait(tempty0 + 8 * acc, acc_phase ^ 1, p.status, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!warp_wait(full0 + 8 * stage, phase, p.status, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(full0 + 8 * stage, phase, p.status, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                if (lane == 0) {
                     const uint32_t a_addr = sA0 + stage * A_STAGE, b_addr = sB0 + stage * B_STAGE;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 32; ++kk) {
+                    for (int kk = 0; kk < BK / 32; ++kk)
                         tc_mma_i8(d, smem_desc_k_sw128(a_addr + kk * 32), smem_desc_k_sw128(b_addr + kk * 32),
                                   IDESC, (kb | kk) != 0);
-                    }
-                    issued = true;
                     tc_commit(empty0 + 8 * stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
                 }
-                if (!ok) break;
-                tc_commit(tfull0 + 8 * acc);
-                if (++acc == NUM_ACC) {
-                    acc = 0;
-                    acc_phase ^= 1;
+                __syncwarp();
+                issued = true;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
                 }
             }
-            if (!ok && issued) {
-                // unwinding: wait for every MMA issued so far before TMEM is freed
+            if (!ok) break;
+            if (lane == 0) tc_commit(tfull0 + 8 * acc);
+            __syncwarp();
+            if (++acc == NUM_ACC) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (!ok && issued) {
+            // unwinding: wait for every MMA issued so far before TMEM is freed
+            if (lane == 0) {
                 tc_commit(drain);
                 mbar_wait(drain, 0, nullptr, nullptr);
             }
         }
+        __syncwarp();
     } else {
         // ------------------------------------------------ epilogue (warps 2..5)
         const int sub = warp & 3;                  // TMEM sub-partition this warp may access
         const int row_in_tile = sub * 32 + lane;
+        const uint32_t epi0 = smem_u32(sEpi) + (uint32_t)((warp - 2) * EPI_BUF);
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t amax = 0;
+        uint32_t qchunk = 0;                       // chunks this warp has staged so far
         const bool vec_ok_f32 = p.out_f32 && (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out_f32) & 15u) == 0);
         const bool vec_ok_i32 = p.out_i32 && (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out_i32) & 15u) == 0);
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
             int tm, tn;
             tile_coords(t, p, tm, tn);
             const int m0 = tm * BM, n0 = tn * BN;
-            // every lane waits, then the warp agrees (and reconverges) before
-            // the warp-collective tcgen05.ld
-            const bool got = mbar_wait(tfull0 + 8 * acc, acc_phase, p.status, abort_flag);
-            if (!__all_sync(0xffffffffu, got)) break;
+            if (!warp_wait(tfull0 + 8 * acc, acc_phase, p.status, abort_flag)) break;
             tc_fence_after();
             const int m = m0 + row_in_tile;
             const bool row_ok = m < p.M;
             float rs = 0.0f;
-            if (p.out_f32 && row_ok) rs = __ldg(p.row_scale + (int64_t)m * p.rs_stride);
             const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
+            // the tile's column scales and bias, staged once per tile in this
+            // warp's own shared-memory slice (read back as broadcasts)
+            float* wcs = sColv + (warp - 2) * 2 * BN;
+            float* wb = wcs + BN;
+            if (p.out_f32) {
+                rs = __ldg(p.row_scale + (int64_t)min(m, p.M - 1) * p.rs_stride);
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    const int nl = min(n0 + c * 32 + lane, p.N - 1);
+                    wcs[c * 32 + lane] = __ldg(p.col_scale + (int64_t)nl * p.cs_stride);
+                    wb[c * 32 + lane] = p.bias ? __ldg(p.bias + nl) : 0.0f;
+                }
+                __syncwarp();
+            }
             for (int c = 0; c < nchunks; ++c) {
                 uint32_t r[32];
-                __syncwarp();
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
                 tc_wait_ld();
-                if (!row_ok) continue;
+                if (c == nchunks - 1) {
+                    // last read of this accumulator: hand it back to the MMA warp now
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+                }
                 const int nb = n0 + c * 32;
-                const bool full_chunk = nb + 32 <= p.N;
-                if (p.out_i32) {
-                    int32_t* dst = p.out_i32 + (int64_t)m * p.ldo + nb;
-                    if (full_chunk && vec_ok_i32) {
+                uint32_t v[32];
+                if (p.out_f32) {
+                    const float4* cs4 = reinterpret_cast<const float4*>(wcs + c * 32);
+                    const float4* b4 = reinterpret_cast<const float4*>(wb + c * 32);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<int4*>(dst + j) =
-                                make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
-                    } else {
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 cs = cs4[j4];
+                        const float csv[4] = {cs.x, cs.y, cs.z, cs.w};
+                        float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        if (p.bias) {
+                            const float4 bb = b4[j4];
+                            bv[0] = bb.x; bv[1] = bb.y; bv[2] = bb.z; bv[3] = bb.w;
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = 4 * j4 + e;
+                            float y = __fmul_rn(__int2float_rn((int)r[j]), rs);
+                            y = __fmul_rn(y, csv[e]);
+                            if (p.bias) y = __fadd_rn(y, bv[e]);
+                            v[j] = __float_as_uint(epi_act_t<ACT>(y));
+                        }
+                    }
+                    if (p.partials && row_ok) {
+                        const int valid = min(32, p.N - nb);
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (nb + j < p.N) dst[j] = (int)r[j];
+                            if (j < valid) amax = max(amax, v[j] & 0x7FFFFFFFu);
                     }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = r[j];
                 }
-                if (p.out_f32) {
-                    float y[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int n = min(nb + j, p.N - 1);
-                        float v = __fmul_rn(__int2float_rn((int)r[j]), rs);
-                        v = __fmul_rn(v, __ldg(p.col_scale + (int64_t)n * p.cs_stride));
-                        if (p.bias) v = __fadd_rn(v, __ldg(p.bias + n));
-                        y[j] = epi_act(v, p.act);
+                if (p.tma_out) {
+                    // stage the warp's 32 x 32 sub-tile (128-byte rows, 128B-swizzled) and TMA-store it
+                    const uint32_t buf = epi0;
+                    if (qchunk >= 1) {
+                        if (lane == 0) bulk_wait_group_read<0>();   // previous store has read the buffer
+                        __syncwarp();
                     }
-                    float* dst = p.out_f32 + (int64_t)m * p.ldo + nb;
-                    if (full_chunk && vec_ok_f32) {
+                    const uint32_t row_addr = buf + (uint32_t)lane * 128u;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            *reinterpret_cast<float4*>(dst + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
-                            amax = max(amax, max(max(__float_as_uint(y[j]) & 0x7FFFFFFFu,
-                                                     __float_as_uint(y[j + 1]) & 0x7FFFFFFFu),
-                                                 max(__float_as_uint(y[j + 2]) & 0x7FFFFFFFu,
-                                                     __float_as_uint(y[j + 3]) & 0x7FFFFFFFu)));
+                    for (int j = 0; j < 8; ++j)
+                        st_shared_v4(row_addr + (uint32_t)((j ^ (lane & 7)) * 16), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                                     v[4 * j + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmOut, buf, nb, m0 + sub * 32);
+                        bulk_commit_group();
+                    }
+                    ++qchunk;
+                } else if (row_ok) {
+                    // direct stores: ragged or unaligned outputs, or both outputs requested
+                    const bool full_chunk = nb + 32 <= p.N;
+                    if (p.out_i32) {
+                        int32_t* dst = p.out_i32 + (int64_t)m * p.ldo + nb;
+                        if (full_chunk && vec_ok_i32) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<int4*>(dst + j) =
+                                    make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (nb + j < p.N) dst[j] = (int)r[j];
                         }
-                    } else {
+                    }
+                    if (p.out_f32) {
+                        float* dst = p.out_f32 + (int64_t)m * p.ldo + nb;
+                        if (full_chunk && vec_ok_f32) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (nb + j < p.N) {
-                                dst[j] = y[j];
-                                amax = max(amax, __float_as_uint(y[j]) & 0x7FFFFFFFu);
-                            }
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(dst + j) =
+                                    make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (nb + j < p.N) dst[j] = __uint_as_float(v[j]);
                         }
                     }
                 }
             }
-            // accumulator drained: hand it back to the MMA warp
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
             if (++acc == NUM_ACC) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
+        if (p.tma_out && lane == 0) bulk_wait_group_all();   // every store landed before exit
+        __syncwarp();
         if (p.partials) {
             amax = warp_max_u32(amax);
             if (lane == 0) red[sub] = amax;
@@ -359,31 +444,62 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D int8 tensor map over rows x cols (cols contiguous), 128-byte swizzle.
-static int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
-                        uint32_t box_rows) {
+// 2-D tensor map over rows x cols (cols contiguous, row pitch `pitch_bytes`), 128-byte swizzle.
+static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t cols, uint64_t rows,
+                        uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return set_error(KZ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols};
+    cuuint64_t strides[1] = {pitch_bytes};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(KZ_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return KZ_OK;
 }
 
-static int ensure_gemm_attrs() {
+static int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                        uint32_t box_rows) {
+    return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, cols, rows, cols, box_cols, box_rows);
+}
+
+static int ensure_gemm_attrs(int dev) {
     static int done[64] = {};
-    int dev = 0;
-    KZ_CHECK_CUDA(cudaGetDevice(&dev));
     if (dev >= 0 && dev < 64 && done[dev]) return KZ_OK;
-    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES));
+    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::SMEM_BYTES));
+    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_RELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::SMEM_BYTES));
+    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::SMEM_BYTES));
     if (dev >= 0 && dev < 64) done[dev] = 1;
     return KZ_OK;
 }
+
+// Tensor maps are encoded on the host; a call that reuses the same buffers and
+// shapes (every step of a serving loop) reuses its maps.  Small per-thread
+// cache keyed by everything the maps encode.
+struct TmapKey {
+    const void* a;
+    const void* b;
+    const void* out;
+    int64_t M, N, K, a_kblock, ldo;
+    int out_kind;
+    int dev;
+    bool operator==(const TmapKey& o) const {
+        return a == o.a && b == o.b && out == o.out && M == o.M && N == o.N && K == o.K && a_kblock == o.a_kblock &&
+               ldo == o.ldo && out_kind == o.out_kind && dev == o.dev;
+    }
+};
+struct TmapEntry {
+    TmapKey key;
+    CUtensorMap a, b, out;
+    bool valid;
+};
+constexpr int kTmapCache = 16;
+thread_local TmapEntry t_tmap_cache[kTmapCache];
+thread_local int t_tmap_next = 0;
 
 }  // namespace kz
 
@@ -452,17 +568,45 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     KZ_REQUIRE(tiles < (1ll << 31), "kz_gemm_i8: too many tiles");
     p.num_tiles = (int)tiles;
 
-    CUtensorMap tmA, tmB;
-    const uint64_t a_rows = (uint64_t)M * (uint64_t)(K / p.a_kblock);
-    st = make_tmap_i8(&tmA, A, (uint64_t)p.a_kblock, a_rows, gemm::BK, gemm::BM);
-    if (st) return st;
-    st = make_tmap_i8(&tmB, B, (uint64_t)K, (uint64_t)N, gemm::BK, gemm::BN);
-    if (st) return st;
-    st = ensure_gemm_attrs();
+    int dev = 0;
+    KZ_CHECK_CUDA(cudaGetDevice(&dev));
+    // TMA-store epilogue when exactly one output is requested and its rows are 16-byte pitched
+    void* out_ptr = out_f32 ? static_cast<void*>(out_f32) : static_cast<void*>(out_i32);
+    p.tma_out = (out_f32 == nullptr) != (out_i32 == nullptr) && (ldo * 4) % 16 == 0 &&
+                (reinterpret_cast<uintptr_t>(out_ptr) & 15u) == 0;
+    const TmapKey key{A, B, out_ptr, M, N, K, p.a_kblock, ldo, p.tma_out ? (out_f32 ? 1 : 2) : 0, dev};
+    TmapEntry* ent = nullptr;
+    for (int i = 0; i < kTmapCache; ++i)
+        if (t_tmap_cache[i].valid && t_tmap_cache[i].key == key) ent = &t_tmap_cache[i];
+    if (!ent) {
+        TmapEntry fresh;
+        memset(&fresh, 0, sizeof(fresh));
+        fresh.key = key;
+        const uint64_t a_rows = (uint64_t)M * (uint64_t)(K / p.a_kblock);
+        st = make_tmap_i8(&fresh.a, A, (uint64_t)p.a_kblock, a_rows, gemm::BK, gemm::BM);
+        if (st) return st;
+        st = make_tmap_i8(&fresh.b, B, (uint64_t)K, (uint64_t)N, gemm::BK, gemm::BN);
+        if (st) return st;
+        if (p.tma_out) {
+            st = make_tmap_2d(&fresh.out, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_INT32,
+                              out_ptr, (uint64_t)N, (uint64_t)M, (uint64_t)ldo * 4, 32, 32);
+            if (st) return st;
+        }
+        fresh.valid = true;
+        ent = &t_tmap_cache[t_tmap_next];
+        *ent = fresh;
+        t_tmap_next = (t_tmap_next + 1) % kTmapCache;
+    }
+    st = ensure_gemm_attrs(dev);
     if (st) return st;
 
     int grid = std::min(p.num_tiles, sm_count());
     if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
-    gemm_i8_kernel<<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(tmA, tmB, p);
+    if (act == KZ_ACT_RELU)
+        gemm_i8_kernel<KZ_ACT_RELU><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
+    else if (act == KZ_ACT_GELU)
+        gemm_i8_kernel<KZ_ACT_GELU><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
+    else
+        gemm_i8_kernel<KZ_ACT_NONE><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
     return launch_status("gemm_i8_kernel");
 }
