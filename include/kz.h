@@ -101,6 +101,19 @@ size_t kz_quantize_cols_workspace_bytes(int64_t K, int64_t N);
 int kz_quantize_cols_f32(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales, float* scales_f32,
                          void* workspace, size_t workspace_bytes, kz_stream_t stream);
 
+/* kz_quantize_cols_f32 for callers that cannot call cudaMalloc (a host
+ * runtime that owns the GPU's memory through its own allocator or arena, or
+ * must not allocate after start-up): same arguments and results, but no
+ * workspace -- its scratch is a static 256 KB device array inside libkz that
+ * every GPU loading the library keeps until exit.  No counterpart in the
+ * reference (it has no device code).  Limits: N <= 65536 output channels
+ * (larger N returns KZ_ERR_INVALID_ARGUMENT).  All calls share the array, so
+ * calls that overlap on the GPU race: order them on one stream.  The first
+ * call on each device resolves the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture. */
+int kz_quantize_cols_f32_noalloc(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales,
+                                 float* scales_f32, kz_stream_t stream);
+
 /* Per-row (per-token) quantize of x[M, K]: row m gets its own scale,
  * quantize.py:66-70 applied to each row. */
 int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double* scales, float* scales_f32,

@@ -38,6 +38,7 @@ SIGNATURES = {
     "kz_quantize_tensor_f32": (_I, [_P, _I64, _P, _P, _P, _P, _P]),
     "kz_quantize_cols_workspace_bytes": (_SZ, [_I64, _I64]),
     "kz_quantize_cols_f32": (_I, [_P, _I64, _I64, _P, _P, _P, _P, _SZ, _P]),
+    "kz_quantize_cols_f32_noalloc": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "kz_quantize_rows_f32": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "kz_dequantize_i8_f32": (_I, [_P, _I64, _D, _P, _P]),
     "kz_dequantize_cols_i8_f32": (_I, [_P, _I64, _I64, _P, _P, _P]),

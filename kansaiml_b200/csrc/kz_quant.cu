@@ -19,6 +19,7 @@
 // t - rint(t) is computed exactly (Sterbenz).  When 1/scale does not fit fp32
 // (max|x| < 2^-100) every element takes the exact path.
 #include <cfloat>
+#include <mutex>
 
 #include "kz_common.cuh"
 
@@ -481,3 +482,87 @@ int kz_dequantize_cols_i8_f32(const int8_t* qT, int64_t K, int64_t N, const doub
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Per-channel weight quantize that allocates nothing.
+//
+// Some callers of this library cannot call cudaMalloc: a host runtime that
+// owns all of the GPU's memory through its own allocator or fixed arena (a
+// JVM, Go or game-engine host binding this C ABI, an inference server that
+// must not allocate after start-up), where an unplanned cudaMalloc would
+// fragment or exceed the memory that host reserved.  For them,
+// kz_quantize_cols_f32_noalloc takes no workspace argument: its scratch (the
+// column-absmax partial maxima) lives in the file-scope device array below.
+//
+// The array is 65536 words (256 KB).  Every GPU that loads libkz holds it until
+// the process exits.  N is limited to 65536 output channels; larger N is
+// rejected with KZ_ERR_INVALID_ARGUMENT.
+//
+// All calls share this one array.  Each call overwrites every entry it later
+// reads (and zeroes the entries it reads when K == 0), so nothing from an
+// earlier call leaks into a result.  Calls whose kernels overlap on the GPU --
+// two streams, or two host threads -- race on the array: order them on one
+// stream or serialise them.
+//
+// Host code must not use the array's name as a device pointer: on the host it
+// is only a stand-in.  The first call on each device, with that device
+// current, resolves the device address with cudaGetSymbolAddress (checked) and
+// caches it; that set-up runs once per device, so make the first call on a
+// device before any stream capture.
+// ----------------------------------------------------------------------------
+
+namespace kz {
+constexpr int64_t kNoAllocScratchWords = 65536;
+static __device__ __align__(256) uint32_t g_noalloc_cols_scratch[kNoAllocScratchWords];
+
+static std::mutex g_noalloc_mu;
+static uint32_t* g_noalloc_ptr[64] = {};
+
+static int noalloc_scratch(uint32_t** out) {
+    int dev = 0;
+    KZ_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(KZ_ERR_UNSUPPORTED_DEVICE, "device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_cols_scratch);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_cols_scratch)");
+        g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return KZ_OK;
+}
+}  // namespace kz
+
+extern "C" int kz_quantize_cols_f32_noalloc(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales,
+                                            float* scales_f32, kz_stream_t stream) {
+    KZ_REQUIRE(K >= 0 && N >= 0, "kz_quantize_cols_f32_noalloc: K and N must be >= 0");
+    KZ_REQUIRE(N <= kz::kNoAllocScratchWords,
+               "kz_quantize_cols_f32_noalloc: N exceeds 65536 output channels, the size of its static scratch; "
+               "use kz_quantize_cols_f32 with a workspace");
+    if (N == 0) return KZ_OK;
+    KZ_REQUIRE(scales != nullptr, "kz_quantize_cols_f32_noalloc: scales is NULL");
+    KZ_REQUIRE(K == 0 || (w && qT), "kz_quantize_cols_f32_noalloc: w or qT is NULL");
+    const int64_t ktiles = K == 0 ? 1 : (K + 127) / 128;
+    KZ_REQUIRE(ktiles < 65536, "kz_quantize_cols_f32_noalloc: K too large");
+    int st = check_device();
+    if (st) return st;
+    uint32_t* partial = nullptr;
+    st = kz::noalloc_scratch(&partial);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int64_t splits = K == 0 ? 1 : col_splits(K, N);
+    if (splits * N > kz::kNoAllocScratchWords) splits = kz::kNoAllocScratchWords / N;
+    if (K == 0) {
+        KZ_CHECK_CUDA(cudaMemsetAsync(partial, 0, (size_t)N * sizeof(uint32_t), s));
+    } else {
+        const int64_t rows_per_split = (K + splits - 1) / splits;
+        absmax_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)splits), dim3(32, 8), 0, s>>>(
+            w, K, N, rows_per_split, partial);
+        st = launch_status("absmax_cols_kernel (noalloc)");
+        if (st) return st;
+    }
+    quantize_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)ktiles), dim3(32, 8), 0, s>>>(
+        w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
+    return launch_status("quantize_cols_kernel (noalloc)");
+}
