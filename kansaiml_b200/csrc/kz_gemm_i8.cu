@@ -5,21 +5,25 @@
 // x.matmul(w)) once both operands are int8; the reference itself has no int8
 // GEMM (quantize.py:35-44) and runs an fp32 loop (backend/cpu/src/Ops.cpp:328-337).
 //
-// Design (one CTA per SM, persistent over output tiles):
-//   tile 128 x 256 (M x N), k-block 128 bytes = one 128-byte swizzle atom;
-//   warp 0      TMA producer: A[128 x 128] and B[256 x 128] per k-block into a
-//               4-stage shared-memory ring (48 KB per stage), no multicast;
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 int32 accumulators)
-//               and one thread issues tcgen05.mma.kind::i8 (M128 N256 K32, four
-//               per k-block), committing each stage back to the producer and
-//               each finished accumulator to the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each warp owns the
-//               32 TMEM lanes = tile rows of its sub-partition), rescale, bias,
-//               activation, store; the second accumulator lets the next tile's
-//               main loop run while this tile drains.
+// Two forms of one persistent, warp-specialised kernel (one CTA per SM):
+//   PAIR   a CTA pair (cluster of 2) owns a 256 x 256 output tile: each CTA
+//          loads 128 rows of A and 128 rows of B per 128-byte k-block (32 KB,
+//          6-stage ring), the leader issues tcgen05.mma.cta_group::2.kind::i8
+//          (M256 N256 K32) that reads both CTAs' shared memory, and each CTA's
+//          TMEM holds its own 128 x 256 int32 accumulator rows.  Per SM this
+//          needs 64 B/cycle of TMA fill for 8192 MAC/cycle.
+//   single one CTA owns a 128 x 256 tile (A 16 KB + B 32 KB per k-block, 4
+//          stages, tcgen05.mma.cta_group::1 M128 N256 K32); used when M <= 128.
+// Roles: warp 0 TMA producer; warp 1 TMEM allocation (512 columns = two
+// accumulators) and, in the leader, the MMA issue (one lane) with commits back
+// to both CTAs' stage barriers and accumulator barriers; warps 2..5 epilogue:
+// tcgen05.ld 32 columns at a time (each warp owns the 32 TMEM lanes of its
+// sub-partition), fp32 rescale / bias / activation with the tile's column
+// scales staged in shared memory, 128B-swizzled staging and a
+// cp.async.bulk.tensor store per 32 x 32 sub-tile.  The second accumulator
+// lets tile i+1's main loop run under tile i's epilogue.  No TMA multicast.
 // Every mbarrier wait is bounded (kz_common.cuh); on expiry the CTA records
-// KZ_ERR_DEVICE_TIMEOUT, unwinds, drains its in-flight copies and MMAs with
-// bounded waits and frees its TMEM.
+// KZ_ERR_DEVICE_TIMEOUT and unwinds.
 #include <cudaTypedefs.h>
 
 #include <cstring>
@@ -30,22 +34,30 @@
 namespace kz {
 
 namespace gemm {
-constexpr int BM = 128, BN = 256, BK = 128;
-constexpr int STAGES = 4;
-constexpr int A_STAGE = BM * BK;   // 16 KB
-constexpr int B_STAGE = BN * BK;   // 32 KB
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int BN = 256, BK = 128;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;                         // two per TMEM sub-partition, one per column half
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int GROUP_M = 16;        // tile rasterisation: 16 tile-rows per group
-constexpr int EPI_WARPS = 4;
 constexpr int EPI_BUF = 32 * 32 * 4;                 // one warp's 32 x 32 fp32/int32 sub-tile
-constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;       // one staging buffer per warp: 16 KB
-constexpr int NUM_BARS = 2 * STAGES + 2 * NUM_ACC + 1;
-constexpr int COLV_BYTES = EPI_WARPS * 2 * BN * 4;      // per warp: the tile's column scales and bias
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + COLV_BYTES + 256;
-constexpr uint32_t IDESC = idesc_i8(BM, BN);
+constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;       // one staging buffer per warp: 32 KB
+constexpr int COLV_BYTES = 2 * BN * 4;               // the tile's column scales and bias (shared by the epilogue)
+
+template <bool PAIR>
+struct Cfg {
+    static constexpr int BM_CTA = 128;                 // accumulator / A rows per CTA
+    static constexpr int BM_TILE = PAIR ? 256 : 128;   // output rows per tile
+    static constexpr int BN_CTA = PAIR ? 128 : 256;    // B rows loaded per CTA
+    static constexpr int A_STAGE = BM_CTA * BK;        // 16 KB
+    static constexpr int B_STAGE = BN_CTA * BK;        // 16 / 32 KB
+    static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 * NUM_ACC + 1;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + COLV_BYTES + 256;   // base 1024-aligned
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+    static constexpr uint32_t IDESC = idesc_i8(BM_TILE, BN);
+};
 }  // namespace gemm
 
 struct GemmParams {
@@ -77,6 +89,13 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm,
     tn = r / gm;
 }
 
+// First k-block of tile t.  Tiles that run at the same time start their k
+// loops at different k-blocks, so the SMs sharing an A row-band or a B
+// column-band do not all fetch the same L2 lines in the same moment.  The
+// int32 accumulation is exact, so the order of the k-blocks does not change
+// the result.
+__device__ __forceinline__ int k_rotation(int t, const GemmParams& p) { return (int)(((unsigned)t * 7u) % (unsigned)p.num_kb); }
+
 template <int ACT>
 __device__ __forceinline__ float epi_act_t(float v) {
     if constexpr (ACT == KZ_ACT_RELU) return v > 0.0f ? v : 0.0f;
@@ -96,42 +115,57 @@ __device__ __forceinline__ float epi_act(float v, int act) {
     return v;
 }
 
-// Whole-warp bounded wait: every lane polls, then the warp agrees.
+// Whole-warp bounded wait: every lane polls, then the warp agrees.  Pair mode
+// waits with cluster-scope acquire (arrivals released by the other CTA).
+template <bool CLUSTER>
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* status, volatile int* abort_flag) {
-    const bool got = mbar_wait(bar, parity, status, abort_flag);
+    const bool got = CLUSTER ? mbar_wait_cluster(bar, parity, status, abort_flag)
+                             : mbar_wait(bar, parity, status, abort_flag);
     return __all_sync(0xffffffffu, got);
 }
 
-template <int ACT>
+template <int ACT, bool PAIR>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
     using namespace gemm;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    using C = Cfg<PAIR>;
+    // The kernel has no static shared memory, so the dynamic region starts at
+    // the base of the CTA's shared window, which is 1024-byte aligned (the
+    // 128B-swizzle atoms need it).  Checked; a misaligned base records an error.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if (smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0) record_status(p.status, KZ_ERR_INVALID_ARGUMENT);
+        return;
+    }
+    uint8_t* smem = smem_raw;
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * A_STAGE;
-    uint8_t* sEpi = sB + STAGES * B_STAGE;
+    uint8_t* sB = smem + C::STAGES * C::A_STAGE;
+    uint8_t* sEpi = sB + C::STAGES * C::B_STAGE;
     float* sColv = reinterpret_cast<float*>(sEpi + EPI_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES + COLV_BYTES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    uint32_t* red = tmem_slot + 2;   // 4 words: epilogue absmax per warp
+    uint32_t* red = tmem_slot + 2;   // EPI_WARPS words: epilogue absmax per warp
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
-    const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NUM_ACC);
-    const uint32_t drain = smem_u32(bars + 2 * STAGES + 2 * NUM_ACC);
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;     // scheduling unit: pair or CTA
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + C::STAGES);
+    const uint32_t tfull0 = smem_u32(bars + 2 * C::STAGES), tempty0 = smem_u32(bars + 2 * C::STAGES + NUM_ACC);
+    const uint32_t drain = smem_u32(bars + 2 * C::STAGES + 2 * NUM_ACC);
     const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
         for (int a = 0; a < NUM_ACC; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, EPI_WARPS);   // one arrive per epilogue warp
+            mbar_init(tempty0 + 8 * a, PAIR ? 2 * EPI_WARPS : EPI_WARPS);   // one arrive per epilogue warp
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -143,13 +177,24 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         if (p.tma_out) tma_prefetch_desc(&tmOut);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync(); else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the leader's barriers (TMA completion, accumulator release) and the
+    // peer's (the leader's commits), as cluster addresses
+    const uint32_t full_lead0 = PAIR ? mapa_shared(full0, 0) : full0;
+    const uint32_t tempty_lead0 = PAIR ? mapa_shared(tempty0, 0) : tempty0;
+    const uint32_t empty_peer0 = PAIR ? mapa_shared(empty0, 1) : empty0;
+    const uint32_t tfull_peer0 = PAIR ? mapa_shared(tfull0, 1) : tfull0;
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (whole warp, lane 0 issues)
@@ -157,145 +202,184 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         uint32_t phase = 0;
         uint32_t armed_mask = 0, armed_phase = 0;   // per stage: armed at least once / parity of last arm
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        for (int t = unit; ok && t < p.num_tiles; t += units) {
             int tm, tn;
             tile_coords(t, p, tm, tn);
-            const int m0 = tm * BM, n0 = tn * BN;
+            const int m0 = tm * C::BM_TILE + (int)rank * C::BM_CTA;   // this CTA's A rows
+            const int nb0 = tn * BN + (int)rank * C::BN_CTA;          // this CTA's B rows
+            const int rot = k_rotation(t, p);
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!warp_wait(empty0 + 8 * stage, phase ^ 1, p.status, abort_flag)) {
+                if (!warp_wait<false>(empty0 + 8 * stage, phase ^ 1, p.status, abort_flag)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(full0 + 8 * stage, STAGE_BYTES);
-                    const int kbyte = kb * BK;
+                    if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, (PAIR ? 2 : 1) * C::STAGE_BYTES);
+                    int kr = kb + rot;
+                    if (kr >= p.num_kb) kr -= p.num_kb;
+                    const int kbyte = kr * BK;
                     int ax = kbyte, ay = m0;
                     if (p.a_kblock != p.K) {
                         const int g = kbyte / p.a_kblock;
                         ax = kbyte - g * p.a_kblock;
                         ay = g * p.M + m0;
                     }
-                    tma_load_2d(sA0 + stage * A_STAGE, &tmA, full0 + 8 * stage, ax, ay);
-                    tma_load_2d(sB0 + stage * B_STAGE, &tmB, full0 + 8 * stage, kbyte, n0);
+                    if constexpr (PAIR) {
+                        tma_load_2d_pair(sA0 + stage * C::A_STAGE, &tmA, full_lead0 + 8 * stage, ax, ay);
+                        tma_load_2d_pair(sB0 + stage * C::B_STAGE, &tmB, full_lead0 + 8 * stage, kbyte, nb0);
+                    } else {
+                        tma_load_2d(sA0 + stage * C::A_STAGE, &tmA, full0 + 8 * stage, ax, ay);
+                        tma_load_2d(sB0 + stage * C::B_STAGE, &tmB, full0 + 8 * stage, kbyte, nb0);
+                    }
                 }
                 __syncwarp();
                 armed_mask |= 1u << stage;
                 armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
-                if (++stage == STAGES) {
+                if (++stage == C::STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
         }
-        if (!ok) {
-            // unwinding: let every armed copy land before the CTA exits
-            for (int s = 0; s < STAGES; ++s)
+        if (!ok && leader) {
+            // unwinding: let every armed copy land before the pair exits
+            for (int s = 0; s < C::STAGES; ++s)
                 if (armed_mask >> s & 1u) mbar_wait(full0 + 8 * s, armed_phase >> s & 1u, nullptr, nullptr);
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer (whole warp, lane 0 issues)
-        int stage = 0;
-        uint32_t phase = 0;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        bool ok = true;
-        bool issued = false;
-        for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-            if (!warp_wait(tempty0 + 8 * acc, acc_phase ^ 1, p.status, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!warp_wait(full0 + 8 * stage, phase, p.status, abort_flag)) {
+        // ------------------------------------------------ MMA issuer (leader; whole warp, lane 0 issues)
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int t = unit; ok && t < p.num_tiles; t += units) {
+                if (!warp_wait<PAIR>(tempty0 + 8 * acc, acc_phase ^ 1, p.status, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a_addr = sA0 + stage * A_STAGE, b_addr = sB0 + stage * B_STAGE;
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!warp_wait<false>(full0 + 8 * stage, phase, p.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    // TMA (async proxy) -> MMA (async proxy) through the mbarrier:
+                    // no tcgen05 fence here; one after the accumulator wait per tile
+                    if (lane == 0) {
+                        const uint32_t a_addr = sA0 + stage * C::A_STAGE, b_addr = sB0 + stage * C::B_STAGE;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 32; ++kk)
-                        tc_mma_i8(d, smem_desc_k_sw128(a_addr + kk * 32), smem_desc_k_sw128(b_addr + kk * 32),
-                                  IDESC, (kb | kk) != 0);
-                    tc_commit(empty0 + 8 * stage);
+                        for (int kk = 0; kk < BK / 32; ++kk) {
+                            const uint64_t da = smem_desc_k_sw128(a_addr + kk * 32);
+                            const uint64_t db = smem_desc_k_sw128(b_addr + kk * 32);
+                            if constexpr (PAIR)
+                                tc_mma_i8_pair(d, da, db, C::IDESC, (kb | kk) != 0);
+                            else
+                                tc_mma_i8(d, da, db, C::IDESC, (kb | kk) != 0);
+                        }
+                        if constexpr (PAIR) {
+                            tc_commit_pair(empty0 + 8 * stage);
+                            tc_commit_pair(empty_peer0 + 8 * stage);
+                        } else {
+                            tc_commit(empty0 + 8 * stage);
+                        }
+                    }
+                    __syncwarp();
+                    issued = true;
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                if (lane == 0) {
+                    if constexpr (PAIR) {
+                        tc_commit_pair(tfull0 + 8 * acc);
+                        tc_commit_pair(tfull_peer0 + 8 * acc);
+                    } else {
+                        tc_commit(tfull0 + 8 * acc);
+                    }
                 }
                 __syncwarp();
-                issued = true;
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
+                if (++acc == NUM_ACC) {
+                    acc = 0;
+                    acc_phase ^= 1;
                 }
             }
-            if (!ok) break;
-            if (lane == 0) tc_commit(tfull0 + 8 * acc);
-            __syncwarp();
-            if (++acc == NUM_ACC) {
-                acc = 0;
-                acc_phase ^= 1;
-            }
-        }
-        if (!ok && issued) {
-            // unwinding: wait for every MMA issued so far before TMEM is freed
-            if (lane == 0) {
-                tc_commit(drain);
-                mbar_wait(drain, 0, nullptr, nullptr);
+            if (!ok && issued) {
+                // unwinding: wait for every MMA issued so far before TMEM is freed
+                if (lane == 0) {
+                    if constexpr (PAIR) tc_commit_pair(drain); else tc_commit(drain);
+                    mbar_wait(drain, 0, nullptr, nullptr);
+                }
             }
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------ epilogue (warps 2..5)
-        const int sub = warp & 3;                  // TMEM sub-partition this warp may access
-        const int row_in_tile = sub * 32 + lane;
-        const uint32_t epi0 = smem_u32(sEpi) + (uint32_t)((warp - 2) * EPI_BUF);
+        // ------------------------------------------------ epilogue (warps 2 .. 2 + EPI_WARPS)
+        // warp w reads TMEM sub-partition (w & 3), i.e. tile rows 32 (w & 3) .. +31
+        // of this CTA, and column half (w - 2) / 4 of the 256-column tile.
+        const int ew = warp - 2;
+        const int sub = warp & 3;
+        const int half = ew >> 2;
+        const int row_in_tile = (int)rank * C::BM_CTA + sub * 32 + lane;
+        const uint32_t epi0 = smem_u32(sEpi) + (uint32_t)(ew * EPI_BUF);
+        float* tcs = sColv;          // [BN] column scales of the current tile
+        float* tb = sColv + BN;      // [BN] bias
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t amax = 0;
         uint32_t qchunk = 0;                       // chunks this warp has staged so far
         const bool vec_ok_f32 = p.out_f32 && (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out_f32) & 15u) == 0);
         const bool vec_ok_i32 = p.out_i32 && (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out_i32) & 15u) == 0);
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        constexpr int CH_PER_WARP = BN / 32 / 2;   // 4 chunks of 32 columns per column half
+        // After a timed-out wait a warp stays "not alive" but keeps walking the
+        // tile loop, so every epilogue warp executes the same named barriers.
+        bool alive = true;
+        for (int t = unit; t < p.num_tiles; t += units) {
             int tm, tn;
             tile_coords(t, p, tm, tn);
-            const int m0 = tm * BM, n0 = tn * BN;
-            if (!warp_wait(tfull0 + 8 * acc, acc_phase, p.status, abort_flag)) break;
-            tc_fence_after();
+            const int m0 = tm * C::BM_TILE, n0 = tn * BN;
             const int m = m0 + row_in_tile;
             const bool row_ok = m < p.M;
             float rs = 0.0f;
             const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
-            // the tile's column scales and bias, staged once per tile in this
-            // warp's own shared-memory slice (read back as broadcasts)
-            float* wcs = sColv + (warp - 2) * 2 * BN;
-            float* wb = wcs + BN;
+            const int c_begin = half * CH_PER_WARP;
+            const int c_end = min(c_begin + CH_PER_WARP, nchunks);
+            // stage the tile's column scales and bias once for all epilogue warps
             if (p.out_f32) {
                 rs = __ldg(p.row_scale + (int64_t)min(m, p.M - 1) * p.rs_stride);
-                __syncwarp();
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    const int nl = min(n0 + c * 32 + lane, p.N - 1);
-                    wcs[c * 32 + lane] = __ldg(p.col_scale + (int64_t)nl * p.cs_stride);
-                    wb[c * 32 + lane] = p.bias ? __ldg(p.bias + nl) : 0.0f;
-                }
-                __syncwarp();
+                asm volatile("bar.sync 2, %0;" ::"n"(32 * EPI_WARPS) : "memory");   // previous tile's readers done
+                const int nl = min(n0 + ew * 32 + lane, p.N - 1);
+                tcs[ew * 32 + lane] = __ldg(p.col_scale + (int64_t)nl * p.cs_stride);
+                tb[ew * 32 + lane] = p.bias ? __ldg(p.bias + nl) : 0.0f;
+                asm volatile("bar.sync 2, %0;" ::"n"(32 * EPI_WARPS) : "memory");
             }
-            for (int c = 0; c < nchunks; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+            if (alive) alive = warp_wait<PAIR>(tfull0 + 8 * acc, acc_phase, p.status, abort_flag);
+            if (!alive) continue;
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
+            uint32_t ra[32], rb[32];
+            if (c_begin < c_end) {
+                tmem_ld_32x32b_x32(tbase + (uint32_t)(c_begin * 32), ra);
                 tc_wait_ld();
-                if (c == nchunks - 1) {
-                    // last read of this accumulator: hand it back to the MMA warp now
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
-                }
+            }
+            for (int c = c_begin; c < c_end; ++c) {
+                // the next chunk's TMEM load runs while this chunk is processed
+                const bool more = c + 1 < c_end;
+                uint32_t r[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = ra[j];
+                if (more) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), rb);
                 const int nb = n0 + c * 32;
                 uint32_t v[32];
                 if (p.out_f32) {
-                    const float4* cs4 = reinterpret_cast<const float4*>(wcs + c * 32);
-                    const float4* b4 = reinterpret_cast<const float4*>(wb + c * 32);
+                    const float4* cs4 = reinterpret_cast<const float4*>(tcs + c * 32);
+                    const float4* b4 = reinterpret_cast<const float4*>(tb + c * 32);
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 cs = cs4[j4];
@@ -339,7 +423,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmOut, buf, nb, m0 + sub * 32);
+                        tma_store_2d(&tmOut, buf, nb, m0 + (int)rank * C::BM_CTA + sub * 32);
                         bulk_commit_group();
                     }
                     ++qchunk;
@@ -374,6 +458,18 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                         }
                     }
                 }
+                if (more) {
+                    tc_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ra[j] = rb[j];
+                }
+            }
+            // every read of this accumulator by this warp is complete: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_cluster(tempty_lead0 + 8 * acc);
+                else mbar_arrive(tempty0 + 8 * acc);
             }
             if (++acc == NUM_ACC) {
                 acc = 0;
@@ -384,19 +480,22 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         __syncwarp();
         if (p.partials) {
             amax = warp_max_u32(amax);
-            if (lane == 0) red[sub] = amax;
-            asm volatile("bar.sync 1, 128;" ::: "memory");   // epilogue warps only
-            if (warp == 2 && lane == 0) {
-                p.partials[1 + blockIdx.x] = max(max(red[0], red[1]), max(red[2], red[3]));
+            if (lane == 0) red[ew] = amax;
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");   // epilogue warps only
+            if (ew == 0 && lane == 0) {
+                uint32_t mx = 0;
+                for (int w = 0; w < EPI_WARPS; ++w) mx = max(mx, red[w]);
+                p.partials[1 + blockIdx.x] = mx;
                 if (blockIdx.x == 0) p.partials[0] = gridDim.x;
             }
         }
     }
 
-    __syncthreads();
+    tc_fence_before();
+    if constexpr (PAIR) cluster_sync(); else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS); else tmem_dealloc(tmem_base, TMEM_COLS);
     }
 }
 
@@ -464,15 +563,23 @@ static int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint6
     return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, cols, rows, cols, box_cols, box_rows);
 }
 
+template <int ACT, bool PAIR>
+static int set_smem_attr() {
+    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<ACT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::Cfg<PAIR>::SMEM_BYTES));
+    return KZ_OK;
+}
+
 static int ensure_gemm_attrs(int dev) {
     static int done[64] = {};
     if (dev >= 0 && dev < 64 && done[dev]) return KZ_OK;
-    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::SMEM_BYTES));
-    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_RELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::SMEM_BYTES));
-    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KZ_ACT_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::SMEM_BYTES));
+    int st = set_smem_attr<KZ_ACT_NONE, false>();
+    if (!st) st = set_smem_attr<KZ_ACT_RELU, false>();
+    if (!st) st = set_smem_attr<KZ_ACT_GELU, false>();
+    if (!st) st = set_smem_attr<KZ_ACT_NONE, true>();
+    if (!st) st = set_smem_attr<KZ_ACT_RELU, true>();
+    if (!st) st = set_smem_attr<KZ_ACT_GELU, true>();
+    if (st) return st;
     if (dev >= 0 && dev < 64) done[dev] = 1;
     return KZ_OK;
 }
@@ -486,10 +593,11 @@ struct TmapKey {
     const void* out;
     int64_t M, N, K, a_kblock, ldo;
     int out_kind;
+    int pair;
     int dev;
     bool operator==(const TmapKey& o) const {
         return a == o.a && b == o.b && out == o.out && M == o.M && N == o.N && K == o.K && a_kblock == o.a_kblock &&
-               ldo == o.ldo && out_kind == o.out_kind && dev == o.dev;
+               ldo == o.ldo && out_kind == o.out_kind && pair == o.pair && dev == o.dev;
     }
 };
 struct TmapEntry {
@@ -500,6 +608,50 @@ struct TmapEntry {
 constexpr int kTmapCache = 16;
 thread_local TmapEntry t_tmap_cache[kTmapCache];
 thread_local int t_tmap_next = 0;
+
+template <int ACT, bool PAIR>
+static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const GemmParams& p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(gemm::THREADS);
+    cfg.dynamicSmemBytes = gemm::Cfg<PAIR>::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {};
+    if (PAIR) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<ACT, PAIR>, ent->a, ent->b, ent->out, p));
+    return KZ_OK;
+}
+
+// How many CTA pairs of the pair kernel can be resident at once (cached per device).
+static int max_active_pairs(int dev) {
+    static int cached[64] = {};
+    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));
+    cfg.blockDim = dim3(gemm::THREADS);
+    cfg.dynamicSmemBytes = gemm::Cfg<true>::SMEM_BYTES;
+    cudaLaunchAttribute attr[1] = {};
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_kernel<KZ_ACT_NONE, true>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+    }
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
+}
 
 }  // namespace kz
 
@@ -561,8 +713,12 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     KZ_REQUIRE(p.a_kblock == K || p.a_kblock % 128 == 0, "kz_gemm_i8: a_kblock must be K or a multiple of 128");
     KZ_REQUIRE((reinterpret_cast<uintptr_t>(A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0,
                "kz_gemm_i8: A and B must be 16-byte aligned");
+    // CTA pairs (256-row tiles) unless the whole problem fits one 128-row tile
+    const bool pair = M > 128 && sm_count() >= 2;
+    const int bm_tile = pair ? gemm::Cfg<true>::BM_TILE : gemm::Cfg<false>::BM_TILE;
+    const int bn_cta = pair ? gemm::Cfg<true>::BN_CTA : gemm::Cfg<false>::BN_CTA;
     p.num_kb = (int)((K + gemm::BK - 1) / gemm::BK);
-    p.tiles_m = (int)((M + gemm::BM - 1) / gemm::BM);
+    p.tiles_m = (int)((M + bm_tile - 1) / bm_tile);
     p.tiles_n = (int)((N + gemm::BN - 1) / gemm::BN);
     const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
     KZ_REQUIRE(tiles < (1ll << 31), "kz_gemm_i8: too many tiles");
@@ -574,7 +730,7 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     void* out_ptr = out_f32 ? static_cast<void*>(out_f32) : static_cast<void*>(out_i32);
     p.tma_out = (out_f32 == nullptr) != (out_i32 == nullptr) && (ldo * 4) % 16 == 0 &&
                 (reinterpret_cast<uintptr_t>(out_ptr) & 15u) == 0;
-    const TmapKey key{A, B, out_ptr, M, N, K, p.a_kblock, ldo, p.tma_out ? (out_f32 ? 1 : 2) : 0, dev};
+    const TmapKey key{A, B, out_ptr, M, N, K, p.a_kblock, ldo, p.tma_out ? (out_f32 ? 1 : 2) : 0, pair ? 1 : 0, dev};
     TmapEntry* ent = nullptr;
     for (int i = 0; i < kTmapCache; ++i)
         if (t_tmap_cache[i].valid && t_tmap_cache[i].key == key) ent = &t_tmap_cache[i];
@@ -583,9 +739,9 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
         memset(&fresh, 0, sizeof(fresh));
         fresh.key = key;
         const uint64_t a_rows = (uint64_t)M * (uint64_t)(K / p.a_kblock);
-        st = make_tmap_i8(&fresh.a, A, (uint64_t)p.a_kblock, a_rows, gemm::BK, gemm::BM);
+        st = make_tmap_i8(&fresh.a, A, (uint64_t)p.a_kblock, a_rows, gemm::BK, 128);
         if (st) return st;
-        st = make_tmap_i8(&fresh.b, B, (uint64_t)K, (uint64_t)N, gemm::BK, gemm::BN);
+        st = make_tmap_i8(&fresh.b, B, (uint64_t)K, (uint64_t)N, gemm::BK, (uint32_t)bn_cta);
         if (st) return st;
         if (p.tma_out) {
             st = make_tmap_2d(&fresh.out, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_INT32,
@@ -600,13 +756,20 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     st = ensure_gemm_attrs(dev);
     if (st) return st;
 
-    int grid = std::min(p.num_tiles, sm_count());
-    if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
-    if (act == KZ_ACT_RELU)
-        gemm_i8_kernel<KZ_ACT_RELU><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
-    else if (act == KZ_ACT_GELU)
-        gemm_i8_kernel<KZ_ACT_GELU><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
-    else
-        gemm_i8_kernel<KZ_ACT_NONE><<<grid, gemm::THREADS, gemm::SMEM_BYTES, s>>>(ent->a, ent->b, ent->out, p);
-    return launch_status("gemm_i8_kernel");
+    int grid;
+    if (pair) {
+        const int pairs = std::min(p.num_tiles, max_active_pairs(dev));
+        grid = 2 * pairs;
+    } else {
+        grid = std::min(p.num_tiles, sm_count());
+    }
+    if (grid > KZ_PARTIALS_WORDS - 1) grid = (KZ_PARTIALS_WORDS - 2) & ~1;
+    if (pair) {
+        if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, true>(grid, s, ent, p);
+        if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, true>(grid, s, ent, p);
+        return launch_gemm<KZ_ACT_NONE, true>(grid, s, ent, p);
+    }
+    if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, false>(grid, s, ent, p);
+    if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, false>(grid, s, ent, p);
+    return launch_gemm<KZ_ACT_NONE, false>(grid, s, ent, p);
 }
