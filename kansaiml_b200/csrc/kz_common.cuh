@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "kz.h"
 
@@ -37,6 +38,25 @@ int check_device();
     do {                                                                \
         if (!(cond)) return ::kz::set_error(KZ_ERR_INVALID_ARGUMENT, msg); \
     } while (0)
+
+// Launches `kernel` on `stream` with programmatic dependent launch enabled:
+// the kernel's prologue may overlap the previous kernel in the stream; the
+// kernel itself calls griddep_wait() before its main work.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1] = {};
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Launch-status check after a <<<>>> launch.
 inline int launch_status(const char* what) {
@@ -129,6 +149,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
             dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
         : "memory");
+}
+
+// ---- programmatic dependent launch
+// Wait until the grid this kernel depends on has completed and its memory is
+// visible (a no-op when the kernel was launched without the PDL attribute).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to start launching (it still waits in
+// griddep_wait for this grid to complete before touching memory).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---- clusters (CTA pairs)

@@ -189,6 +189,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if constexpr (PAIR) cluster_sync(); else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the prologue above overlaps the previous kernel (programmatic dependent
+    // launch); from here on A, the scales and the output may be touched
+    griddep_launch_dependents();
+    griddep_wait();
     // the leader's barriers (TMA completion, accumulator release) and the
     // peer's (the leader's commits), as cluster addresses
     const uint32_t full_lead0 = PAIR ? mapa_shared(full0, 0) : full0;
@@ -616,14 +620,17 @@ static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const Gem
     cfg.blockDim = dim3(gemm::THREADS);
     cfg.dynamicSmemBytes = gemm::Cfg<PAIR>::SMEM_BYTES;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1] = {};
+    cudaLaunchAttribute attr[2] = {};
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (PAIR) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
     }
     KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<ACT, PAIR>, ent->a, ent->b, ent->out, p));
     return KZ_OK;

@@ -36,6 +36,8 @@ __device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v
 // the count.  NaN bit patterns exceed +Inf's, so they survive the max.
 __global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ x, int64_t n,
                                                      uint32_t* __restrict__ partials) {
+    griddep_launch_dependents();
+    griddep_wait();
     uint32_t m = 0;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
@@ -44,19 +46,20 @@ __global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ x
         const int64_t nv = n >> 2;
         const float4* xv = reinterpret_cast<const float4*>(x);
         int64_t i = tid;
-        // four independent 16-byte loads in flight per thread
+        // four independent 16-byte loads in flight per thread; default caching
+        // keeps x in L2 for the quantize pass that follows
         for (; i + 3 * nthreads < nv; i += 4 * nthreads) {
-            float4 a = __ldcs(xv + i);
-            float4 b = __ldcs(xv + i + nthreads);
-            float4 c = __ldcs(xv + i + 2 * nthreads);
-            float4 d = __ldcs(xv + i + 3 * nthreads);
+            float4 a = __ldg(xv + i);
+            float4 b = __ldg(xv + i + nthreads);
+            float4 c = __ldg(xv + i + 2 * nthreads);
+            float4 d = __ldg(xv + i + 3 * nthreads);
             m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
             m = max(m, max(max(abs_bits(b.x), abs_bits(b.y)), max(abs_bits(b.z), abs_bits(b.w))));
             m = max(m, max(max(abs_bits(c.x), abs_bits(c.y)), max(abs_bits(c.z), abs_bits(c.w))));
             m = max(m, max(max(abs_bits(d.x), abs_bits(d.y)), max(abs_bits(d.z), abs_bits(d.w))));
         }
         for (; i < nv; i += nthreads) {
-            float4 a = __ldcs(xv + i);
+            float4 a = __ldg(xv + i);
             m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
         }
         for (int64_t j = (nv << 2) + tid; j < n; j += nthreads) m = max(m, abs_bits(x[j]));
@@ -142,6 +145,8 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
                                                                 const uint32_t* __restrict__ partials,
                                                                 int8_t* __restrict__ q, double* scale_out,
                                                                 float* scale_f32_out, int* status) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t bits = block_reduce_partials(partials);
     const ScaleInfo si = scale_from_absmax_bits(bits);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -174,7 +179,7 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
             o.y = pack4(b, si);
             o.z = pack4(c, si);
             o.w = pack4(d, si);
-            __stcs(qv + i, o);
+            qv[i] = o;   // default policy: the int8 GEMM reads the codes next
         }
         for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
     } else {
@@ -370,8 +375,8 @@ int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t str
     int grid = elementwise_grid((n + 15) / 16);
     if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
     if (grid > 4 * sm_count()) grid = 4 * sm_count();
-    absmax_kernel<<<grid, 256, 0, s>>>(x, n, partials);
-    return launch_status("absmax_kernel");
+    KZ_CHECK_CUDA(launch_pdl(absmax_kernel, dim3(grid), dim3(256), 0, s, x, n, partials));
+    return KZ_OK;
 }
 
 int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials, int8_t* q, double* scale,
@@ -382,9 +387,9 @@ int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    quantize_partials_kernel<<<elementwise_grid((n + 15) / 16), 256, 0, s>>>(x, n, partials, q, scale, scale_f32,
-                                                                              device_status_ptr());
-    return launch_status("quantize_partials_kernel");
+    KZ_CHECK_CUDA(launch_pdl(quantize_partials_kernel, dim3(elementwise_grid((n + 15) / 16)), dim3(256), 0, s, x, n,
+                             partials, q, scale, scale_f32, device_status_ptr()));
+    return KZ_OK;
 }
 
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
