@@ -46,11 +46,17 @@ enum kz_status_code {
 enum kz_activation { KZ_ACT_NONE = 0, KZ_ACT_RELU = 1, KZ_ACT_GELU = 2 };
 
 /* Words in an absmax `partials` buffer (uint32_t[KZ_PARTIALS_WORDS]).
- * Word 0 holds the number of valid partials P; words 1..P hold the bit
- * patterns of non-negative fp32 partial maxima (|x| as uint32 bits, so
- * unsigned max == float max, and NaN sorts above +Inf).  Because the
- * partials are plain maxima, an element-wise integer MAX all-reduce of the
- * buffer across ranks yields the global absmax (config 5). */
+ * Word 0 holds the number of valid partials P (P <= KZ_PARTIALS_WORDS - 3);
+ * words 1..P hold the bit patterns of non-negative fp32 partial maxima (|x| as
+ * uint32 bits, so unsigned max == float max, and NaN sorts above +Inf).
+ * Because the partials are plain maxima, an element-wise integer MAX
+ * all-reduce of words 0..P across ranks yields the global absmax (config 5).
+ * The last two words are the grid barrier of kz_quantize_tensor_f32's
+ * single-launch form (an arrival counter and a generation word): ZERO-FILL A
+ * BUFFER ONCE BEFORE ITS FIRST USE; every completed call returns the counter
+ * to zero and advances the generation word.  One buffer per stream
+ * (calls on one stream are ordered; calls on different streams must not share
+ * a buffer). */
 #define KZ_PARTIALS_WORDS 1024
 
 /* ------------------------------------------------------------------ misc */
@@ -87,8 +93,11 @@ int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t str
 int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials, int8_t* q,
                              double* scale, float* scale_f32, kz_stream_t stream);
 
-/* quantize_symmetric (quantize.py:50-70) on the device: kz_absmax_f32 then
- * kz_quantize_partials_f32; `partials` is caller scratch. */
+/* quantize_symmetric (quantize.py:50-70) on the device.  Large tensors run as
+ * ONE cooperative launch (absmax, a bounded grid barrier in the last two words
+ * of `partials`, quantize while x is still in L2); small ones as
+ * kz_absmax_f32 + kz_quantize_partials_f32.  `partials` is caller scratch,
+ * zero-filled before its first use (see KZ_PARTIALS_WORDS). */
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
                            uint32_t* partials, kz_stream_t stream);
 

@@ -710,7 +710,7 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
 
     if (K == 0) {
         int grid = (int)std::min<int64_t>((M * N + 255) / 256, (int64_t)sm_count() * 4);
-        if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
+        if (grid > KZ_PARTIALS_WORDS - 3) grid = KZ_PARTIALS_WORDS - 3;
         gemm_i8_k0_kernel<<<grid, 256, 0, s>>>(p);
         return launch_status("gemm_i8_k0_kernel");
     }
@@ -770,7 +770,7 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     } else {
         grid = std::min(p.num_tiles, sm_count());
     }
-    if (grid > KZ_PARTIALS_WORDS - 1) grid = (KZ_PARTIALS_WORDS - 2) & ~1;
+    if (grid > KZ_PARTIALS_WORDS - 3) grid = (KZ_PARTIALS_WORDS - 3) & ~1;
     if (pair) {
         if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, true>(grid, s, ent, p);
         if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, true>(grid, s, ent, p);

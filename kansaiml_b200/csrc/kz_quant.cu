@@ -18,6 +18,14 @@
 // elements (about 1 in 2000 for smooth data) take the exact double division.
 // t - rint(t) is computed exactly (Sterbenz).  When 1/scale does not fit fp32
 // (max|x| < 2^-100) every element takes the exact path.
+//
+// The fast path rounds with one fp32 add: y = t + 1.5 * 2^23 lies in
+// [2^23, 2^24) where floats are the integers, so the add itself rounds t half
+// to even, y - 1.5 * 2^23 = rint(t) exactly, and y's bit pattern is
+// 0x4B400000 + rint(t), whose low byte is the two's-complement int8 code.  No
+// clamp is needed: |t| <= 127 * (1 + 2^-23) * (1 + 2^-24) < 127.5 - 2^-12, so
+// rint(t) is in [-127, 127] and never near the 127.5 tie.
+#include <algorithm>
 #include <cfloat>
 #include <mutex>
 
@@ -46,17 +54,15 @@ __global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ x
         const int64_t nv = n >> 2;
         const float4* xv = reinterpret_cast<const float4*>(x);
         int64_t i = tid;
-        // four independent 16-byte loads in flight per thread; default caching
+        // eight independent 16-byte loads in flight per thread; default caching
         // keeps x in L2 for the quantize pass that follows
-        for (; i + 3 * nthreads < nv; i += 4 * nthreads) {
-            float4 a = __ldg(xv + i);
-            float4 b = __ldg(xv + i + nthreads);
-            float4 c = __ldg(xv + i + 2 * nthreads);
-            float4 d = __ldg(xv + i + 3 * nthreads);
-            m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
-            m = max(m, max(max(abs_bits(b.x), abs_bits(b.y)), max(abs_bits(b.z), abs_bits(b.w))));
-            m = max(m, max(max(abs_bits(c.x), abs_bits(c.y)), max(abs_bits(c.z), abs_bits(c.w))));
-            m = max(m, max(max(abs_bits(d.x), abs_bits(d.y)), max(abs_bits(d.z), abs_bits(d.w))));
+        for (; i + 7 * nthreads < nv; i += 8 * nthreads) {
+            float4 a[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a[u] = __ldg(xv + i + u * nthreads);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                m = max(m, max(max(abs_bits(a[u].x), abs_bits(a[u].y)), max(abs_bits(a[u].z), abs_bits(a[u].w))));
         }
         for (; i < nv; i += nthreads) {
             float4 a = __ldg(xv + i);
@@ -115,7 +121,26 @@ __device__ __forceinline__ int8_t quant_one(float v, const ScaleInfo& si) {
     return quant_exact(v, si.scale);
 }
 
+constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
+
+// Four codes packed little-endian into one word.  One tie check per four
+// elements; the rare word with a near-tie element falls back per element.
 __device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) {
+    if (si.fast) {
+        const float t0 = __fmul_rn(v.x, si.rcp), t1 = __fmul_rn(v.y, si.rcp);
+        const float t2 = __fmul_rn(v.z, si.rcp), t3 = __fmul_rn(v.w, si.rcp);
+        const float y0 = __fadd_rn(t0, kRoundMagic), y1 = __fadd_rn(t1, kRoundMagic);
+        const float y2 = __fadd_rn(t2, kRoundMagic), y3 = __fadd_rn(t3, kRoundMagic);
+        const float d0 = fabsf(__fsub_rn(t0, __fsub_rn(y0, kRoundMagic)));
+        const float d1 = fabsf(__fsub_rn(t1, __fsub_rn(y1, kRoundMagic)));
+        const float d2 = fabsf(__fsub_rn(t2, __fsub_rn(y2, kRoundMagic)));
+        const float d3 = fabsf(__fsub_rn(t3, __fsub_rn(y3, kRoundMagic)));
+        if (fmaxf(fmaxf(d0, d1), fmaxf(d2, d3)) <= kTieGuard) {
+            const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
+            const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
+            return __byte_perm(lo01, lo23, 0x5410);
+        }
+    }
     uint32_t b0 = (uint8_t)quant_one(v.x, si), b1 = (uint8_t)quant_one(v.y, si);
     uint32_t b2 = (uint8_t)quant_one(v.z, si), b3 = (uint8_t)quant_one(v.w, si);
     return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
@@ -125,7 +150,7 @@ __device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) 
 __device__ __forceinline__ uint32_t block_reduce_partials(const uint32_t* __restrict__ partials) {
     __shared__ uint32_t red[32];
     __shared__ uint32_t result;
-    const uint32_t count = min(partials[0], (uint32_t)(KZ_PARTIALS_WORDS - 1));
+    const uint32_t count = min(partials[0], (uint32_t)(KZ_PARTIALS_WORDS - 3));
     uint32_t m = 0;
     for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) m = max(m, partials[1 + i]);
     m = warp_max_u32(m);
@@ -180,6 +205,139 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
             o.z = pack4(c, si);
             o.w = pack4(d, si);
             qv[i] = o;   // default policy: the int8 GEMM reads the codes next
+        }
+        for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
+    }
+}
+
+// ----------------------------------------- fused absmax + quantize (1 launch)
+
+// Words of the partials buffer the fused kernel uses as its grid barrier
+// (arrival counter and generation).  They must be zero before the first use of
+// a buffer; every completed launch leaves them at zero again.
+constexpr int kBarrierCtr = KZ_PARTIALS_WORDS - 2;
+constexpr int kBarrierGen = KZ_PARTIALS_WORDS - 1;
+constexpr int kFusedMaxBlocks = KZ_PARTIALS_WORDS - 3;
+
+// Bounded grid barrier for a cooperative launch (all blocks co-resident).
+// Returns false after recording KZ_ERR_DEVICE_TIMEOUT when it runs out.
+__device__ __forceinline__ bool grid_barrier(uint32_t* partials, int* status) {
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        volatile uint32_t* gen = partials + kBarrierGen;
+        const uint32_t g0 = *gen;                       // read before arriving
+        __threadfence();                                // this block's partial is visible
+        const uint32_t old = atomicAdd(partials + kBarrierCtr, 1u);
+        ok = 1;
+        if (old == gridDim.x - 1) {
+            atomicExch(partials + kBarrierCtr, 0u);     // leave the counter at zero
+            __threadfence();
+            atomicAdd(partials + kBarrierGen, 1u);
+        } else {
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t it = 0;
+            while (*gen == g0) {
+                if ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                    record_status(status, KZ_ERR_DEVICE_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// One launch: phase 1 writes each block's partial absmax, a grid barrier, then
+// phase 2 reduces the partials, derives the scale and quantizes (x is re-read
+// while still in L2).  Same arithmetic as absmax_kernel + quantize_partials_kernel.
+__global__ void __launch_bounds__(1024, 1) quantize_fused_kernel(const float* __restrict__ x, int64_t n,
+                                                             uint32_t* __restrict__ partials, int8_t* __restrict__ q,
+                                                             double* scale_out, float* scale_f32_out, int* status) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+    const float4* xv = reinterpret_cast<const float4*>(x);
+    // phase 1: block absmax
+    uint32_t m = 0;
+    if (aligned) {
+        const int64_t nv = n >> 2;
+        int64_t i = tid;
+        for (; i + 7 * nthreads < nv; i += 8 * nthreads) {
+            float4 a[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a[u] = __ldg(xv + i + u * nthreads);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                m = max(m, max(max(abs_bits(a[u].x), abs_bits(a[u].y)), max(abs_bits(a[u].z), abs_bits(a[u].w))));
+        }
+        for (; i < nv; i += nthreads) {
+            const float4 a = __ldg(xv + i);
+            m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
+        }
+        for (int64_t j = (nv << 2) + tid; j < n; j += nthreads) m = max(m, abs_bits(x[j]));
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) m = max(m, abs_bits(x[j]));
+    }
+    m = warp_max_u32(m);
+    __shared__ uint32_t red[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) {
+            partials[1 + blockIdx.x] = v;
+            if (blockIdx.x == 0) partials[0] = gridDim.x;
+        }
+    }
+    if (!grid_barrier(partials, status)) return;
+    // phase 2: global absmax -> scale -> codes
+    uint32_t bits = 0;
+    for (uint32_t i = threadIdx.x; i < gridDim.x; i += blockDim.x) bits = max(bits, __ldcg(partials + 1 + i));
+    bits = warp_max_u32(bits);
+    __syncthreads();
+    if (lane == 0) red[warp] = bits;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    const ScaleInfo si = scale_from_absmax_bits(red[0]);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (si.finite) {
+            *scale_out = si.scale;
+            if (scale_f32_out) *scale_f32_out = __double2float_rn(si.scale);
+        } else {
+            *scale_out = __longlong_as_double(0x7FF8000000000000ll);
+            if (scale_f32_out) *scale_f32_out = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    if (!si.finite) {
+        for (int64_t j = tid; j < n; j += nthreads) q[j] = 0;
+        return;
+    }
+    if (aligned) {
+        const int64_t n16 = n >> 4;
+        uint4* qv = reinterpret_cast<uint4*>(q);
+        for (int64_t i = tid; i < n16; i += nthreads) {
+            const float4 a = __ldcs(xv + 4 * i), b = __ldcs(xv + 4 * i + 1);
+            const float4 c = __ldcs(xv + 4 * i + 2), d = __ldcs(xv + 4 * i + 3);
+            uint4 o;
+            o.x = pack4(a, si);
+            o.y = pack4(b, si);
+            o.z = pack4(c, si);
+            o.w = pack4(d, si);
+            qv[i] = o;
         }
         for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
     } else {
@@ -372,9 +530,9 @@ int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t str
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int grid = elementwise_grid((n + 15) / 16);
-    if (grid > KZ_PARTIALS_WORDS - 1) grid = KZ_PARTIALS_WORDS - 1;
-    if (grid > 4 * sm_count()) grid = 4 * sm_count();
+    int grid = (int)std::min<int64_t>((n + 32 * 256 - 1) / (32 * 256), 6 * (int64_t)sm_count());
+    if (grid < 1) grid = 1;
+    if (grid > KZ_PARTIALS_WORDS - 3) grid = KZ_PARTIALS_WORDS - 3;
     KZ_CHECK_CUDA(launch_pdl(absmax_kernel, dim3(grid), dim3(256), 0, s, x, n, partials));
     return KZ_OK;
 }
@@ -392,11 +550,47 @@ int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials
     return KZ_OK;
 }
 
+static int fused_grid(int dev) {
+    static int cached[64] = {};
+    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_fused_kernel, 1024, 0) != cudaSuccess)
+        per_sm = 0;
+    int g = std::min(per_sm, 1) * sm_count();   // one 1024-thread block per SM: few barrier arrivals
+    if (g > kFusedMaxBlocks) g = kFusedMaxBlocks;
+    if (dev >= 0 && dev < 64) cached[dev] = g;
+    return g;
+}
+
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
                            uint32_t* partials, kz_stream_t stream) {
-    int st = kz_absmax_f32(x, n, partials, stream);
+    KZ_REQUIRE(n >= 0, "kz_quantize_tensor_f32: n must be >= 0");
+    KZ_REQUIRE(partials && scale, "kz_quantize_tensor_f32: partials and scale must be non-NULL");
+    KZ_REQUIRE(n == 0 || (x && q), "kz_quantize_tensor_f32: x or q is NULL");
+    int st = check_device();
     if (st) return st;
-    return kz_quantize_partials_f32(x, n, partials, q, scale, scale_f32, stream);
+    int dev = 0;
+    KZ_CHECK_CUDA(cudaGetDevice(&dev));
+    const int grid = fused_grid(dev);
+    if (grid < 1 || n < (int64_t)1 << 16) {
+        // small tensors: the two-kernel form (no grid barrier needed)
+        st = kz_absmax_f32(x, n, partials, stream);
+        if (st) return st;
+        return kz_quantize_partials_f32(x, n, partials, q, scale, scale_f32, stream);
+    }
+    const int g = (int)std::min<int64_t>(grid, (n + 16383) / 16384);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)g);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1] = {};
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, quantize_fused_kernel, x, n, partials, q, scale, scale_f32,
+                                     device_status_ptr()));
+    return KZ_OK;
 }
 
 static int64_t col_splits(int64_t K, int64_t N) {

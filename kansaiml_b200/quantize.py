@@ -39,13 +39,19 @@ _ACTS = {None: _lib.KZ_ACT_NONE, "none": _lib.KZ_ACT_NONE, "relu": _lib.KZ_ACT_R
 _partials_cache = {}
 
 
+def new_partials(device):
+    """A zero-filled KZ_PARTIALS_WORDS buffer (the fused quantize keeps its
+    grid barrier in the last two words, which must start at zero)."""
+    return torch.zeros(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=device)
+
+
 def partials_buffer(device):
     """A KZ_PARTIALS_WORDS scratch buffer private to (device, current stream):
     calls on one stream are ordered, so they may share it."""
     key = (device.index, stream_handle(device))
     buf = _partials_cache.get(key)
     if buf is None:
-        buf = torch.empty(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=device)
+        buf = new_partials(device)
         _partials_cache[key] = buf
     return buf
 
@@ -87,7 +93,7 @@ def quantize_partials_device(x, partials):
 def absmax_partials_device(x, partials=None):
     dev = x.device
     if partials is None:
-        partials = torch.empty(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+        partials = new_partials(dev)
     _lib.call("kz_absmax_f32", ptr(x), x.numel(), ptr(partials), stream_handle(dev))
     return partials
 

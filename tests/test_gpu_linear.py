@@ -143,7 +143,7 @@ def test_gemm_epilogue_vs_oracle(k, act, per_row):
     rsc = rs.uniform(1e-3, 1e-2, M if per_row else 1).astype(np.float32)
     csc = rs.uniform(1e-3, 1e-2, N).astype(np.float32)
     bias = rs.standard_normal(N).astype(np.float32)
-    partials = torch.empty(1024, dtype=torch.int32, device="cuda")
+    partials = torch.zeros(1024, dtype=torch.int32, device="cuda")
     y, acc = kq.gemm_i8_device(dev(a), dev(b), row_scale=dev(rsc), col_scale=dev(csc), bias=dev(bias), act=act,
                                out_i32=torch.empty((M, N), dtype=torch.int32, device="cuda"), partials=partials)
     acc_o = ocpu.gemm_i8(a, b)

@@ -175,3 +175,31 @@ def test_dequantize_per_channel_roundtrip(kq):
     ref = (qo.T.astype(np.float64) * so[None, :]).astype(np.float32)
     assert deq.tobytes() == ref.tobytes()
     assert np.all(np.abs(deq - w) <= (so[None, :] / 2 + 1e-7))
+
+
+def test_fused_single_launch_repeated_calls(kq):
+    """Large tensors take the single cooperative launch (absmax, grid barrier,
+    quantize).  Repeated calls on one partials buffer stay bit-exact; each call
+    returns the barrier's arrival counter (second-to-last word) to zero and
+    advances its generation word (last word) by one."""
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    partials = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    calls = 0
+    for seed, n, scale in [(0, 1 << 22, 1.0), (1, (1 << 23) + 13, 1e-3), (2, 3 << 20, 50.0)]:
+        x = (np.random.RandomState(seed).standard_normal(n) * scale).astype(np.float32)
+        xd = dev(x)
+        q = torch.empty(n, dtype=torch.int8, device="cuda")
+        s64 = torch.empty(1, dtype=torch.float64, device="cuda")
+        s32 = torch.empty(1, dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            assert lib.kz_quantize_tensor_f32(xd.data_ptr(), n, q.data_ptr(), s64.data_ptr(), s32.data_ptr(),
+                                              partials.data_ptr(), stream) == 0
+            calls += 1
+        torch.cuda.synchronize()
+        qo, so = ocpu.quantize_tensor(x)
+        assert float(s64.item()) == so
+        np.testing.assert_array_equal(q.cpu().numpy(), qo)
+        assert partials[-2:].cpu().numpy().tolist() == [0, calls]
+    assert kq.device_status() == 0
