@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--workload", choices=["linear", "stack"], default="linear",
+                    help="linear: BASELINE config 2 (default); stack: config 5, column-sharded 4-layer stack")
     return ap.parse_args()
 
 
@@ -234,6 +236,9 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.workload == "stack":
+        run_stack(args, rank, world, local_rank, dev)
+        return
 
     import kansaiml_b200 as kz
     from kansaiml_b200 import _lib
@@ -402,6 +407,80 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": M_TOK * K_IN * 4,
                 "d2h_bytes_per_step": M_TOK * N_OUT * 4},
         "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
+
+
+# ------------------------------------------------- config 5: sharded stack
+
+STACK_M, STACK_D, STACK_L = 8192, 16384, 4
+
+
+def run_stack(args, rank, world, local_rank, dev):
+    """4 int8 Linear layers [16384 -> 16384], weights
+    ~ N(0, 0.01) quantized per output channel and column-sharded over the
+    ranks, activations fp32 [8192, 16384] ~ N(0, 1) quantized per tensor and
+    all-gathered (int8, NCCL over NVLink) between layers.  One step = one
+    forward of the stack over the 8192-token batch; total work fixed as N grows
+    ("strong" scaling).  Output: each rank's fp32 column shard."""
+    import torch
+    import torch.distributed as dist
+
+    from kansaiml_b200.distributed import DeviceMesh, ShardedQLinearStack
+
+    mesh = DeviceMesh.spmd() if world > 1 else None
+
+    def weight(l):
+        g = torch.Generator(device=dev)
+        g.manual_seed(5000 + l)
+        return torch.randn((STACK_D, STACK_D), generator=g, device=dev) * 0.01
+
+    stack = ShardedQLinearStack([weight] * STACK_L, mesh)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    x = torch.randn((STACK_M, STACK_D), generator=g, device=dev)
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        stack(x)
+    K = args.steps
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for _ in range(K):
+            stack(x)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_per_step = ms / K
+    ops = 2.0 * STACK_M * STACK_D * STACK_D * STACK_L
+    tops = ops / (ms_per_step / 1e3) / 1e12
+    hbm_gbs, bf16, _, peak_src = peaks()
+    line = {
+        "metric": METRIC, "value": STACK_M / (ms_per_step / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "config5: 4 x int8 Linear [16384 -> 16384] column-sharded, 8192 tokens, per-tensor "
+                               "activation quant + NCCL all-gather between layers",
+                   "global_batch": STACK_M, "seq_len": None, "parallelism": f"tp{world} (column-sharded weights)",
+                   "l2": "inputs larger than L2 (weights 1 GiB int8 in total, activations 512 MiB fp32)"},
+        "tops": tops,
+        "roofline": {"kernel": "whole stack", "bound": "tensor", "achieved": tops, "peak": 2.0 * bf16 * world,
+                     "unit": "TOP/s", "frac": tops / (2.0 * bf16 * world), "traffic": None,
+                     "peak_source": f"{world} x 2 x bf16_tflops ({bf16:.1f}, {peak_src})"},
+        "gpu_launches": (1 + 2 * STACK_L - 1) * K,
         "clocks": clk.summary(),
     }
     print(json.dumps(line))

@@ -1,0 +1,358 @@
+"""DeviceMesh / DTensor for the int8 path on B200s (python/kansai/distributed.py).
+
+Same names and placement semantics as the reference: ``DeviceMesh``,
+``Shard(dim)`` / ``Replicate()``, ``DTensor.from_tensor`` / ``to_tensor``,
+``_chunk_sizes`` (remainder to the first pieces, distributed.py:157-159),
+``_split_tensor`` / ``_concat_tensors`` (distributed.py:162-182), ``_run_parallel``
+(one thread per device, errors re-raised, distributed.py:73-102) and
+``dtensor_run`` (distributed.py:219-267).  The reference's mesh entries name
+in-process backends ("cpu", "metal") over host memory; here they are GPUs.
+
+Two ways to drive a mesh:
+
+* **one process, several GPUs**: ``DeviceMesh(["cuda:0", "cuda:1"])`` -- the
+  reference's model.  ``DTensor.from_tensor`` splits and places each piece on
+  its device, ``dtensor_run(fn, placement, *dts)`` runs ``fn`` per device on its
+  own thread (libkz and torch release the GIL), ``to_tensor`` concatenates.
+  ``dtensor_run`` takes a callable: the reference's KIR graphs (kir.py) are not
+  part of this path.
+* **one process per GPU** (torchrun): ``DeviceMesh.spmd()`` -- each rank holds
+  its own shard; collectives run on NCCL over NVLink.
+
+``ShardedQLinearStack`` is BASELINE config 5: a stack of int8 Linear layers
+whose weights are column-sharded over the mesh (``Shard(1)`` of the reference's
+[in, out] weight), activations quantized per tensor and all-gathered between
+layers.  Per layer: int8 GEMM of the full activation codes against the local
+weight columns (the epilogue also emits absmax partials of its fp32 output) ->
+integer MAX all-reduce of the partials (the global per-tensor absmax) ->
+quantize the local output columns -> all-gather of the int8 codes into the
+rank-major layout [G][M][N/G], which the next GEMM reads directly (a_kblock =
+N/G).  Sharding changes no arithmetic: the result equals the unsharded stack
+bit for bit.
+"""
+import threading
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .quantize import (QTensor, gemm_i8_device, new_partials, quantize_cols_device, quantize_partials_device,
+                       quantize_tensor_device)
+from .tensor import Tensor, as_tensor, cat
+
+
+# ------------------------------------------------------------ host helpers
+
+def _run_parallel(work_fns):
+    """distributed.py:73-102: one thread per callable, results in order, the
+    first error re-raised after every thread has finished."""
+    results = [None] * len(work_fns)
+    errors = [None] * len(work_fns)
+
+    def runner(i):
+        try:
+            results[i] = work_fns[i]()
+        except Exception as e:  # noqa: BLE001 -- re-raised below
+            errors[i] = e
+
+    threads = [threading.Thread(target=runner, args=(i,)) for i in range(len(work_fns))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for e in errors:
+        if e is not None:
+            raise e
+    return results
+
+
+def _chunk_sizes(total, n):
+    """distributed.py:157-159: as equal as possible, remainder to the first pieces."""
+    base, remainder = divmod(total, n)
+    return [base + 1 if i < remainder else base for i in range(n)]
+
+
+def _split_tensor(tensor, dim, n):
+    sizes = _chunk_sizes(tensor.shape[dim], n)
+    pieces, offset = [], 0
+    for size in sizes:
+        pieces.append(tensor.slice(dim, offset, offset + size))
+        offset += size
+    return pieces
+
+
+def _concat_tensors(tensors, dim):
+    return cat(tensors, dim)
+
+
+def _parse_device(d):
+    if d == "cpu":
+        return torch.device("cpu")
+    if d == "cuda":
+        return torch.device("cuda", 0)
+    if isinstance(d, str) and d.startswith("cuda:") and d[5:].isdigit():
+        return torch.device(d)
+    return None
+
+
+class DeviceMesh:
+    """A 1-D list of devices, one shard each (distributed.py:105-129).
+
+    Entries are "cuda:N" (or "cpu" for data-only use).  In SPMD mode (one
+    process per GPU, ``DeviceMesh.spmd()``) ``devices`` lists every rank's GPU
+    and ``rank`` / ``group`` identify this process."""
+
+    _VALID_DEVICES = ("cuda:N", "cpu")
+
+    def __init__(self, devices):
+        devices = list(devices)
+        parsed = []
+        for d in devices:
+            dev = _parse_device(d)
+            if dev is None:
+                raise ValueError(f"unknown device {d!r} -- kansaiml_b200 meshes take {self._VALID_DEVICES}")
+            if dev.type == "cuda" and (not torch.cuda.is_available() or dev.index >= torch.cuda.device_count()):
+                raise RuntimeError(f"DeviceMesh includes {d!r} but that CUDA device is not available")
+            parsed.append(dev)
+        self.devices = devices
+        self.torch_devices = parsed
+        self.rank = None
+        self.group = None
+
+    @classmethod
+    def spmd(cls, group=None):
+        """The mesh of an initialised torch.distributed job: one GPU per rank."""
+        if not dist.is_initialized():
+            raise RuntimeError("DeviceMesh.spmd() needs torch.distributed to be initialised")
+        world = dist.get_world_size(group)
+        obj = cls.__new__(cls)
+        obj.devices = [f"rank{r}" for r in range(world)]
+        obj.torch_devices = None
+        obj.rank = dist.get_rank(group)
+        obj.group = group
+        return obj
+
+    @property
+    def is_spmd(self):
+        return self.rank is not None
+
+    def __len__(self):
+        return len(self.devices)
+
+    def __repr__(self):
+        return f"DeviceMesh({self.devices})"
+
+
+class Shard:
+    """Split along `dim` into len(mesh) pieces, remainder to the first pieces."""
+
+    def __init__(self, dim):
+        self.dim = dim
+
+    def __repr__(self):
+        return f"Shard({self.dim})"
+
+    def __eq__(self, other):
+        return isinstance(other, Shard) and self.dim == other.dim
+
+
+class Replicate:
+    def __repr__(self):
+        return "Replicate()"
+
+    def __eq__(self, other):
+        return isinstance(other, Replicate)
+
+
+class DTensor:
+    """A tensor sharded or replicated across a DeviceMesh (distributed.py:185-216).
+
+    ``shards[i]`` is mesh device i's piece, resident on that device.  In SPMD
+    mode ``shards`` holds only this rank's piece (``local``)."""
+
+    def __init__(self, mesh, placement, shards):
+        expected = 1 if mesh.is_spmd else len(mesh)
+        if len(shards) != expected:
+            raise ValueError(f"DTensor needs one shard per mesh device ({expected}), got {len(shards)}")
+        self.mesh = mesh
+        self.placement = placement
+        self.shards = list(shards)
+
+    @property
+    def local(self):
+        """This rank's shard (SPMD mode) or the first device's."""
+        return self.shards[0]
+
+    @staticmethod
+    def from_tensor(tensor, mesh, placement):
+        tensor = as_tensor(tensor)
+        if isinstance(placement, Replicate):
+            pieces = [tensor] * (1 if mesh.is_spmd else len(mesh))
+        elif isinstance(placement, Shard):
+            pieces = _split_tensor(tensor, placement.dim, len(mesh))
+            if mesh.is_spmd:
+                pieces = [pieces[mesh.rank]]
+        else:
+            raise TypeError(f"unknown placement {placement!r}")
+        if not mesh.is_spmd:
+            pieces = [p.to(dev) for p, dev in zip(pieces, mesh.torch_devices)]
+        else:
+            here = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+            pieces = [p.to(here) for p in pieces]
+        return DTensor(mesh, placement, pieces)
+
+    def to_tensor(self):
+        """Replicate -> shard 0; Shard(d) -> concatenation (an all-gather in SPMD mode)."""
+        if isinstance(self.placement, Replicate):
+            return self.shards[0]
+        if not isinstance(self.placement, Shard):
+            raise TypeError(f"unknown placement {self.placement!r}")
+        if not self.mesh.is_spmd:
+            first = self.shards[0].device
+            return _concat_tensors([s.to(first) for s in self.shards], self.placement.dim)
+        local = self.shards[0].data.contiguous()
+        sizes = [torch.tensor(list(local.shape), device=local.device)]
+        world = len(self.mesh)
+        all_sizes = [torch.empty_like(sizes[0]) for _ in range(world)]
+        dist.all_gather(all_sizes, sizes[0], group=self.mesh.group)
+        parts = [torch.empty(s.tolist(), dtype=local.dtype, device=local.device) for s in all_sizes]
+        dist.all_gather(parts, local, group=self.mesh.group)
+        return Tensor(torch.cat(parts, self.placement.dim))
+
+    def __repr__(self):
+        return f"DTensor(mesh={self.mesh}, placement={self.placement}, shard_shapes={[s.shape for s in self.shards]})"
+
+
+def dtensor_run(fn, output_placement, *dtensor_args):
+    """distributed.py:219-267 with a callable: ``fn(*shards)`` runs once per
+    mesh device, on its own thread, with that device current."""
+    if callable(fn) is False:
+        raise TypeError("dtensor_run takes a callable (kansaiml_b200 has no KIR graphs)")
+    if not dtensor_args:
+        raise ValueError("dtensor_run needs at least one DTensor argument")
+    mesh = dtensor_args[0].mesh
+    for dt in dtensor_args:
+        if dt.mesh is not mesh:
+            raise ValueError("all DTensor arguments must share the same DeviceMesh")
+    if mesh.is_spmd:
+        return DTensor(mesh, output_placement, [fn(*[dt.shards[0] for dt in dtensor_args])])
+
+    def make(i, dev):
+        shard_inputs = [dt.shards[i] for dt in dtensor_args]
+
+        def work():
+            if dev.type == "cuda":
+                with torch.cuda.device(dev):
+                    out = fn(*shard_inputs)
+                    torch.cuda.current_stream(dev).synchronize()
+                    return out
+            return fn(*shard_inputs)
+        return work
+
+    results = _run_parallel([make(i, dev) for i, dev in enumerate(mesh.torch_devices)])
+    return DTensor(mesh, output_placement, results)
+
+
+# --------------------------------------------------------- collectives
+
+def allreduce_partials_max(partials, group=None):
+    """Element-wise MAX of absmax partials across ranks, in place.  The two
+    grid-barrier words at the end of the buffer are left out."""
+    words = partials[: _lib.KZ_PARTIALS_WORDS - 2]
+    dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group)
+    return partials
+
+
+def allgather_blocked(local, group=None, out=None):
+    """All-gather equally shaped shards into rank-major blocks [G, *local.shape]:
+    the layout the int8 GEMM consumes directly as K blocks."""
+    world = dist.get_world_size(group)
+    if out is None:
+        out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), local.contiguous(), group=group)
+    return out
+
+
+def column_shard_bounds(total, rank, world):
+    """[start, stop) of this rank's columns under Shard(1) (remainder first)."""
+    sizes = _chunk_sizes(total, world)
+    start = sum(sizes[:rank])
+    return start, start + sizes[rank]
+
+
+# -------------------------------------------------- config 5: sharded stack
+
+class ShardedQLinearStack:
+    """A stack of bias-free int8 Linear layers, weights column-sharded over the
+    ranks of an SPMD mesh (or a single GPU when the mesh is None).
+
+    weights: list of fp32 [K, N] tensors (the reference layout), or callables
+    ``w(l)`` returning layer l's full weight on the current device.  Each rank
+    keeps only its columns, quantized per output channel.  N / G must be a
+    multiple of 128 between layers (the GEMM's K block)."""
+
+    def __init__(self, weights, mesh=None):
+        self.mesh = mesh
+        self.world = len(mesh) if mesh is not None and mesh.is_spmd else 1
+        self.rank = mesh.rank if mesh is not None and mesh.is_spmd else 0
+        self.group = mesh.group if mesh is not None and mesh.is_spmd else None
+        self.layers = []
+        for i, w in enumerate(weights):
+            full = w(i) if callable(w) else as_tensor(w).data
+            K, N = full.shape
+            if N % self.world:
+                raise ValueError(f"layer {i}: out_features {N} is not divisible by the mesh size {self.world}")
+            lo, hi = column_shard_bounds(N, self.rank, self.world)
+            shard = full[:, lo:hi].contiguous()
+            del full
+            qT, s64, s32 = quantize_cols_device(shard)
+            del shard
+            qt = QTensor._from_device(qT, s64, s32, [K, hi - lo], "channel")
+            qt._check_finite()
+            self.layers.append((qt, K, N))
+        for i in range(1, len(self.layers)):
+            if self.layers[i][1] != self.layers[i - 1][2]:
+                raise ValueError("consecutive layers' shapes do not chain")
+        if self.world > 1:
+            n_loc = self.layers[0][2] // self.world
+            if n_loc % 128:
+                raise ValueError("out_features / mesh size must be a multiple of 128")
+        self.partials = None
+
+    def forward(self, x, return_local=True):
+        """x: fp32 [M, K] replicated on every rank.  Returns the last layer's
+        fp32 output: this rank's column shard (return_local) or the full
+        [M, N] (all-gathered)."""
+        xd = as_tensor(x).data.contiguous()
+        dev = xd.device
+        if self.partials is None or self.partials.device != dev:
+            self.partials = new_partials(dev)
+        M = xd.shape[0]
+        a, _, a_s32 = quantize_tensor_device(xd)
+        a_kblock = xd.shape[1]
+        y = None
+        for li, (qt, K, N) in enumerate(self.layers):
+            n_loc = qt.shape[1]
+            last = li == len(self.layers) - 1
+            y, _ = gemm_i8_device(a, qt.kmajor(), row_scale=a_s32, col_scale=qt.scale_f32, a_kblock=a_kblock, m=M,
+                                  partials=None if last else self.partials)
+            if last:
+                break
+            if self.world > 1:
+                allreduce_partials_max(self.partials, self.group)
+            yq, _, a_s32 = quantize_partials_device(y, self.partials)
+            if self.world > 1:
+                a = allgather_blocked(yq, self.group)   # [G, M, n_loc]
+                a_kblock = n_loc
+            else:
+                a = yq
+                a_kblock = N
+        if return_local or self.world == 1:
+            return Tensor(y)
+        parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
+        return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+
+    __call__ = forward

@@ -1,0 +1,125 @@
+"""GPU parity of the sharded int8 stack and of DTensor
+dispatch.  Sharding changes no arithmetic, so every configuration must equal
+the oracle's unsharded chain bit for bit:
+
+    a0 = quantize_tensor(x); for each layer: acc = a @ Wq^T (int32),
+    y = epilogue(acc, s_a, s_w) (fp32); (a, s_a) = quantize_tensor(y)
+
+The multi-GPU cases run only where two GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import cpu as ocpu
+
+pytestmark = pytest.mark.gpu
+
+DIMS = [1024, 1024, 2048, 1024]   # in -> ... -> out
+M = 384
+
+
+def make_weights():
+    rs = np.random.RandomState(55)
+    return [(rs.standard_normal((DIMS[i], DIMS[i + 1])) * 0.01).astype(np.float32) for i in range(len(DIMS) - 1)]
+
+
+def make_x():
+    return np.random.RandomState(56).standard_normal((M, DIMS[0])).astype(np.float32)
+
+
+def oracle_chain(x, weights):
+    a, s_a = ocpu.quantize_tensor(x)
+    y = None
+    for i, w in enumerate(weights):
+        wq, ws = ocpu.quantize_cols(w)
+        acc = ocpu.gemm_i8(a, wq)
+        y = ocpu.epilogue(acc, s_a, ws)
+        if i < len(weights) - 1:
+            a, s_a = ocpu.quantize_tensor(y)
+    return y
+
+
+@pytest.fixture(scope="module")
+def expected():
+    return oracle_chain(make_x(), make_weights())
+
+
+def test_stack_single_gpu_bit_exact(cuda_device, expected):
+    from kansaiml_b200.distributed import ShardedQLinearStack
+    stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()])
+    y = stack(torch.from_numpy(make_x()).cuda()).numpy()
+    assert y.tobytes() == expected.tobytes()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _spmd_worker(rank, world, port, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from kansaiml_b200.distributed import DeviceMesh, ShardedQLinearStack
+        mesh = DeviceMesh.spmd()
+        stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh)
+        y = stack(torch.from_numpy(make_x()).cuda(), return_local=False).numpy()
+        q.put((rank, y))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_stack_two_gpus_spmd_bit_exact(expected):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_spmd_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, y = q.get(timeout=300)
+        res[r] = y
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert isinstance(res[r], np.ndarray), res[r]
+        assert res[r].tobytes() == expected.tobytes()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_dtensor_single_process_two_gpus():
+    """The reference's threaded mesh, on two GPUs: batch Shard(0), weight
+    replicated, per-channel W8A8 qlinear on each device, gathered result equal
+    to one device's."""
+    import kansaiml_b200 as kz
+    from kansaiml_b200 import distributed as kd
+    from kansaiml_b200.quantize import QTensor, qlinear
+    w = make_weights()[0]
+    x = make_x()
+    mesh = kd.DeviceMesh(["cuda:0", "cuda:1"])
+    xd = kd.DTensor.from_tensor(kz.from_numpy(x, device="cuda:0"), mesh, kd.Shard(0))
+    wq = {i: QTensor.from_tensor(kz.from_numpy(w, device=f"cuda:{i}"), per_channel=True) for i in range(2)}
+
+    def fwd(xs):
+        return qlinear(xs, wq[xs.device.index])
+    out = kd.dtensor_run(fwd, kd.Shard(0), xd).to_tensor().numpy()
+    whole = qlinear(kz.from_numpy(x, device="cuda:0"), wq[0]).numpy()
+    # per-tensor activation scales differ per shard (each shard is its own
+    # tensor, as in the reference's dtensor_run); compare each half to its own run
+    for i, (lo, hi) in enumerate([(0, M // 2), (M // 2, M)]):
+        part = qlinear(kz.from_numpy(x[lo:hi], device="cuda:0"), wq[0]).numpy()
+        assert out[lo:hi].tobytes() == part.tobytes()
+    assert out.shape == whole.shape
