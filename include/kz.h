@@ -51,10 +51,10 @@ enum kz_activation { KZ_ACT_NONE = 0, KZ_ACT_RELU = 1, KZ_ACT_GELU = 2 };
  * uint32 bits, so unsigned max == float max, and NaN sorts above +Inf).
  * Because the partials are plain maxima, an element-wise integer MAX
  * all-reduce of words 0..P across ranks yields the global absmax (config 5).
- * The last two words are the grid barrier of kz_quantize_tensor_f32's
- * single-launch form (an arrival counter and a generation word): ZERO-FILL A
- * BUFFER ONCE BEFORE ITS FIRST USE; every completed call returns the counter
- * to zero and advances the generation word.  One buffer per stream
+ * The second-to-last word is the grid barrier of kz_quantize_tensor_f32's
+ * single-launch form and the last word is reserved: ZERO-FILL A BUFFER ONCE
+ * BEFORE ITS FIRST USE; every completed single-launch call leaves the low 31
+ * bits of the barrier word at zero and flips its bit 31.  One buffer per stream
  * (calls on one stream are ordered; calls on different streams must not share
  * a buffer). */
 #define KZ_PARTIALS_WORDS 1024

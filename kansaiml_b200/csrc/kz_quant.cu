@@ -25,6 +25,14 @@
 // 0x4B400000 + rint(t), whose low byte is the two's-complement int8 code.  No
 // clamp is needed: |t| <= 127 * (1 + 2^-23) * (1 + 2^-24) < 127.5 - 2^-12, so
 // rint(t) is in [-127, 127] and never near the 127.5 tie.
+//
+// The vector form (pack4) folds the multiply into fused multiply-adds:
+// y = fl32(x*r + 1.5 * 2^23) gives k = y - 1.5 * 2^23, the integer nearest to
+// the exact product x*r, and d = fl32(x*r - k) its residual with one rounding
+// (|fl32(d) - d| <= 2^-25).  |x*r - x/scale| < 127 * 2^-24 < 2^-17, so
+// |fl64(x/scale) - k| <= |fl32(d)| + 2^-16 and |fl32(d)| <= 1/2 - 2^-12 again
+// proves k = rint(fl64(x/scale)).  Only the elements that fail the bound take
+// the exact division.
 #include <algorithm>
 #include <cfloat>
 #include <mutex>
@@ -123,33 +131,52 @@ __device__ __forceinline__ int8_t quant_one(float v, const ScaleInfo& si) {
 
 constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
 
-// Four codes packed little-endian into one word.  One tie check per four
-// elements; the rare word with a near-tie element falls back per element.
-__device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) {
-    if (si.fast) {
-        const float t0 = __fmul_rn(v.x, si.rcp), t1 = __fmul_rn(v.y, si.rcp);
-        const float t2 = __fmul_rn(v.z, si.rcp), t3 = __fmul_rn(v.w, si.rcp);
-        const float y0 = __fadd_rn(t0, kRoundMagic), y1 = __fadd_rn(t1, kRoundMagic);
-        const float y2 = __fadd_rn(t2, kRoundMagic), y3 = __fadd_rn(t3, kRoundMagic);
-        const float d0 = fabsf(__fsub_rn(t0, __fsub_rn(y0, kRoundMagic)));
-        const float d1 = fabsf(__fsub_rn(t1, __fsub_rn(y1, kRoundMagic)));
-        const float d2 = fabsf(__fsub_rn(t2, __fsub_rn(y2, kRoundMagic)));
-        const float d3 = fabsf(__fsub_rn(t3, __fsub_rn(y3, kRoundMagic)));
-        if (fmaxf(fmaxf(d0, d1), fmaxf(d2, d3)) <= kTieGuard) {
-            const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
-            const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
-            return __byte_perm(lo01, lo23, 0x5410);
-        }
-    }
-    uint32_t b0 = (uint8_t)quant_one(v.x, si), b1 = (uint8_t)quant_one(v.y, si);
-    uint32_t b2 = (uint8_t)quant_one(v.z, si), b3 = (uint8_t)quant_one(v.w, si);
-    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+// Code of one element by the fused-multiply-add form (see the file header);
+// *near is set when the element needs the exact path.
+__device__ __forceinline__ uint32_t fma_code(float v, float rcp, bool* near) {
+    const float y = __fmaf_rn(v, rcp, kRoundMagic);
+    const float d = __fmaf_rn(v, rcp, -__fsub_rn(y, kRoundMagic));
+    *near = fabsf(d) > kTieGuard;
+    return __float_as_uint(y) & 0xFFu;
 }
 
-// Reduce a partials buffer inside one block; every thread gets the result.
-__device__ __forceinline__ uint32_t block_reduce_partials(const uint32_t* __restrict__ partials) {
+// Exact-path repair of a packed word: only the near-tie bytes are recomputed,
+// so a warp with one such element pays for one division.  Kept out of line so
+// the hot loops do not carry its registers.
+__device__ __noinline__ uint32_t pack4_repair(float4 v, uint32_t w, double scale, float rcp, bool fast) {
+    const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        bool near = true;
+        if (fast) fma_code(e[j], rcp, &near);
+        if (near) w = (w & ~(0xFFu << (8 * j))) | ((uint32_t)(uint8_t)quant_exact(e[j], scale) << (8 * j));
+    }
+    return w;
+}
+
+// Four codes packed little-endian into one word: three fp32 operations per
+// element and one tie check per four; a word with a near-tie element is
+// repaired per element.
+__device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) {
+    const float y0 = __fmaf_rn(v.x, si.rcp, kRoundMagic), y1 = __fmaf_rn(v.y, si.rcp, kRoundMagic);
+    const float y2 = __fmaf_rn(v.z, si.rcp, kRoundMagic), y3 = __fmaf_rn(v.w, si.rcp, kRoundMagic);
+    const float d0 = __fmaf_rn(v.x, si.rcp, -__fsub_rn(y0, kRoundMagic));
+    const float d1 = __fmaf_rn(v.y, si.rcp, -__fsub_rn(y1, kRoundMagic));
+    const float d2 = __fmaf_rn(v.z, si.rcp, -__fsub_rn(y2, kRoundMagic));
+    const float d3 = __fmaf_rn(v.w, si.rcp, -__fsub_rn(y3, kRoundMagic));
+    const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
+    const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
+    const uint32_t w = __byte_perm(lo01, lo23, 0x5410);
+    const float dm = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3)));
+    if (si.fast && dm <= kTieGuard) return w;
+    return pack4_repair(v, w, si.scale, si.rcp, si.fast);
+}
+
+// Reduce a partials buffer inside one block and derive the scale once (the
+// double divisions run on one thread); every thread gets the result.
+__device__ __forceinline__ ScaleInfo block_scale_from_partials(const uint32_t* __restrict__ partials) {
     __shared__ uint32_t red[32];
-    __shared__ uint32_t result;
+    __shared__ ScaleInfo result;
     const uint32_t count = min(partials[0], (uint32_t)(KZ_PARTIALS_WORDS - 3));
     uint32_t m = 0;
     for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) m = max(m, partials[1 + i]);
@@ -160,7 +187,7 @@ __device__ __forceinline__ uint32_t block_reduce_partials(const uint32_t* __rest
     if (warp == 0) {
         uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
         v = warp_max_u32(v);
-        if (lane == 0) result = v;
+        if (lane == 0) result = scale_from_absmax_bits(v);
     }
     __syncthreads();
     return result;
@@ -172,8 +199,7 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
                                                                 float* scale_f32_out, int* status) {
     griddep_launch_dependents();
     griddep_wait();
-    const uint32_t bits = block_reduce_partials(partials);
-    const ScaleInfo si = scale_from_absmax_bits(bits);
+    const ScaleInfo si = block_scale_from_partials(partials);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         if (si.finite) {
             *scale_out = si.scale;
@@ -214,37 +240,41 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
 
 // ----------------------------------------- fused absmax + quantize (1 launch)
 
-// Words of the partials buffer the fused kernel uses as its grid barrier
-// (arrival counter and generation).  They must be zero before the first use of
-// a buffer; every completed launch leaves them at zero again.
-constexpr int kBarrierCtr = KZ_PARTIALS_WORDS - 2;
-constexpr int kBarrierGen = KZ_PARTIALS_WORDS - 1;
+// Word of the partials buffer the fused kernels use as their grid barrier.
+// It must be zero before the first use of a buffer; every completed launch
+// leaves its low 31 bits at zero and flips bit 31.
+constexpr int kBarrierWord = KZ_PARTIALS_WORDS - 2;
 constexpr int kFusedMaxBlocks = KZ_PARTIALS_WORDS - 3;
 
-// Bounded grid barrier for a cooperative launch (all blocks co-resident).
-// Returns false after recording KZ_ERR_DEVICE_TIMEOUT when it runs out.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded sense-reversal grid barrier for a cooperative launch (all blocks
+// co-resident), one atomic per block: block 0 adds 2^31 - (G - 1), every other
+// block adds 1.  Whatever the arrival order, bit 31 of the word keeps its old
+// value until the G-th arrival and flips with it, and the low 31 bits end where
+// they started (zero).  Each block waits until bit 31 differs from the value
+// it saw on arrival.  Returns false after recording KZ_ERR_DEVICE_TIMEOUT when
+// the wait runs out.
 __device__ __forceinline__ bool grid_barrier(uint32_t* partials, int* status) {
     __shared__ int ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        volatile uint32_t* gen = partials + kBarrierGen;
-        const uint32_t g0 = *gen;                       // read before arriving
+        uint32_t* word = partials + kBarrierWord;
+        const uint32_t add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
         __threadfence();                                // this block's partial is visible
-        const uint32_t old = atomicAdd(partials + kBarrierCtr, 1u);
+        const uint32_t old = atomicAdd(word, add);
         ok = 1;
-        if (old == gridDim.x - 1) {
-            atomicExch(partials + kBarrierCtr, 0u);     // leave the counter at zero
-            __threadfence();
-            atomicAdd(partials + kBarrierGen, 1u);
-        } else {
-            const uint64_t t0 = globaltimer_ns();
-            uint32_t it = 0;
-            while (*gen == g0) {
-                if ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-                    record_status(status, KZ_ERR_DEVICE_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t it = 0;
+        while (((ld_acquire_gpu(word) ^ old) & 0x80000000u) == 0) {
+            if ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_status(status, KZ_ERR_DEVICE_TIMEOUT);
+                ok = 0;
+                break;
             }
         }
         __threadfence();
@@ -305,13 +335,14 @@ __global__ void __launch_bounds__(1024, 1) quantize_fused_kernel(const float* __
     __syncthreads();
     if (lane == 0) red[warp] = bits;
     __syncthreads();
+    __shared__ ScaleInfo s_si;
     if (warp == 0) {
         uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
         v = warp_max_u32(v);
-        if (lane == 0) red[0] = v;
+        if (lane == 0) s_si = scale_from_absmax_bits(v);
     }
     __syncthreads();
-    const ScaleInfo si = scale_from_absmax_bits(red[0]);
+    const ScaleInfo si = s_si;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         if (si.finite) {
             *scale_out = si.scale;
@@ -343,6 +374,122 @@ __global__ void __launch_bounds__(1024, 1) quantize_fused_kernel(const float* __
     } else {
         for (int64_t j = tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
     }
+}
+
+// Shared-memory-resident variant of the fused quantize: block b owns the
+// contiguous chunk [b * chunk, (b + 1) * chunk) of x; the first `cap` bytes of
+// it arrive by bulk copy into shared memory (one HBM read at full bandwidth)
+// and stay there for both passes; any remainder beyond `cap` is read from
+// global memory in both passes.  x and q must be 16-byte aligned and chunk a
+// multiple of 16 elements.
+constexpr int kResidentBlock = 1024;
+constexpr uint32_t kBulkPiece = 32768;
+
+__global__ void __launch_bounds__(kResidentBlock, 1)
+    quantize_resident_kernel(const float* __restrict__ x, int64_t n, int64_t chunk, uint32_t cap_floats,
+                             uint32_t* __restrict__ partials, int8_t* __restrict__ q, double* scale_out,
+                             float* scale_f32_out, int* status) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    float* xs = reinterpret_cast<float*>(smem_raw);
+    __shared__ uint64_t bar;
+    __shared__ uint32_t red[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t e0 = blockIdx.x * chunk;
+    const int64_t e1 = min(n, e0 + chunk);
+    const int64_t len = max((int64_t)0, e1 - e0);
+    const uint32_t res = (uint32_t)min((int64_t)cap_floats, len & ~(int64_t)3);   // resident floats (x4)
+    const uint32_t bar_addr = smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(bar_addr, 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+    griddep_wait();
+    if (threadIdx.x == 0 && res > 0) {
+        mbar_arrive_expect_tx(bar_addr, res * 4u);
+        const char* src = reinterpret_cast<const char*>(x + e0);
+        for (uint32_t off = 0; off < res * 4u; off += kBulkPiece)
+            bulk_load(smem_u32(smem_raw) + off, src + off, min(kBulkPiece, res * 4u - off), bar_addr);
+    }
+    // phase 1: absmax of the non-resident remainder while the copy is in flight.
+    // When res < len the remainder starts at e0 + cap, a multiple of 16 elements.
+    uint32_t m = 0;
+    const int64_t r0 = e0 + res;
+    const int64_t rem4 = (e1 - r0) >> 2;
+    const float4* xr4 = reinterpret_cast<const float4*>(x + r0);
+    for (int64_t i = threadIdx.x; i < rem4; i += blockDim.x) {
+        const float4 a = __ldg(xr4 + i);
+        m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
+    }
+    for (int64_t j = r0 + 4 * rem4 + threadIdx.x; j < e1; j += blockDim.x) m = max(m, abs_bits(x[j]));
+    bool ok = true;
+    if (res > 0) ok = mbar_wait(bar_addr, 0, status, nullptr);
+    if (ok) {
+        const float4* xs4 = reinterpret_cast<const float4*>(xs);
+        for (uint32_t i = threadIdx.x; i < res / 4; i += blockDim.x) {
+            const float4 a = xs4[i];
+            m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
+        }
+    }
+    m = warp_max_u32(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) {
+            partials[1 + blockIdx.x] = v;
+            if (blockIdx.x == 0) partials[0] = gridDim.x;
+        }
+    }
+    if (!grid_barrier(partials, status) || !ok) return;
+    // phase 2: global absmax -> scale -> codes from shared memory
+    uint32_t bits = 0;
+    for (uint32_t i = threadIdx.x; i < gridDim.x; i += blockDim.x) bits = max(bits, __ldcg(partials + 1 + i));
+    bits = warp_max_u32(bits);
+    __syncthreads();
+    if (lane == 0) red[warp] = bits;
+    __syncthreads();
+    __shared__ ScaleInfo s_si;
+    if (warp == 0) {
+        uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+        v = warp_max_u32(v);
+        if (lane == 0) s_si = scale_from_absmax_bits(v);
+    }
+    __syncthreads();
+    const ScaleInfo si = s_si;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (si.finite) {
+            *scale_out = si.scale;
+            if (scale_f32_out) *scale_f32_out = __double2float_rn(si.scale);
+        } else {
+            *scale_out = __longlong_as_double(0x7FF8000000000000ll);
+            if (scale_f32_out) *scale_f32_out = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    if (!si.finite) {
+        for (int64_t j = e0 + threadIdx.x; j < e1; j += blockDim.x) q[j] = 0;
+        return;
+    }
+    // resident part: consecutive threads read consecutive 16 B of shared memory
+    // (no bank conflicts) and store 4 codes each (128 B per warp).
+    const float4* xs4 = reinterpret_cast<const float4*>(xs);
+    uint32_t* qw = reinterpret_cast<uint32_t*>(q + e0);
+    constexpr uint32_t B = kResidentBlock;
+    uint32_t i = threadIdx.x;
+    for (; i + 3 * B < res / 4; i += 4 * B) {
+        const float4 a0 = xs4[i], a1 = xs4[i + B], a2 = xs4[i + 2 * B], a3 = xs4[i + 3 * B];
+        qw[i] = pack4(a0, si);
+        qw[i + B] = pack4(a1, si);
+        qw[i + 2 * B] = pack4(a2, si);
+        qw[i + 3 * B] = pack4(a3, si);
+    }
+    for (; i < res / 4; i += B) qw[i] = pack4(xs4[i], si);
+    uint32_t* qr = reinterpret_cast<uint32_t*>(q + r0);
+    for (int64_t i = threadIdx.x; i < rem4; i += blockDim.x) qr[i] = pack4(__ldcs(xr4 + i), si);
+    for (int64_t j = r0 + 4 * rem4 + threadIdx.x; j < e1; j += blockDim.x) q[j] = quant_one(x[j], si);
 }
 
 // ------------------------------------------------------ per-column (weights)
@@ -428,17 +575,17 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
     for (int64_t j = threadIdx.x; j < K; j += blockDim.x) m = max(m, abs_bits(xr[j]));
     m = warp_max_u32(m);
     __shared__ uint32_t red[32];
-    __shared__ uint32_t res;
+    __shared__ ScaleInfo res;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) red[warp] = m;
     __syncthreads();
     if (warp == 0) {
         uint32_t v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
         v = warp_max_u32(v);
-        if (lane == 0) res = v;
+        if (lane == 0) res = scale_from_absmax_bits(v);
     }
     __syncthreads();
-    const ScaleInfo si = scale_from_absmax_bits(res);
+    const ScaleInfo si = res;
     if (threadIdx.x == 0) {
         if (si.finite) {
             scales[row] = si.scale;
@@ -577,6 +724,40 @@ int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, 
         st = kz_absmax_f32(x, n, partials, stream);
         if (st) return st;
         return kz_quantize_partials_f32(x, n, partials, q, scale, scale_f32, stream);
+    }
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+    if (aligned) {
+        // one block per SM, its chunk resident in shared memory
+        static int smem_set[64] = {};
+        int max_smem = 0;
+        KZ_CHECK_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        const int dyn = max_smem - 1024;   // leave room for the kernel's static shared memory
+        if (dev >= 0 && dev < 64 && !smem_set[dev]) {
+            KZ_CHECK_CUDA(cudaFuncSetAttribute(quantize_resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+            smem_set[dev] = 1;
+        }
+        const int G = std::min(sm_count(), kFusedMaxBlocks);
+        int64_t chunk = (n + G - 1) / G;
+        chunk = (chunk + 15) / 16 * 16;
+        const uint32_t cap = (uint32_t)((dyn / 4) & ~15);
+        cudaLaunchConfig_t rcfg = {};
+        rcfg.gridDim = dim3((unsigned)G);
+        rcfg.blockDim = dim3(kResidentBlock);
+        rcfg.dynamicSmemBytes = (size_t)dyn;
+        rcfg.stream = reinterpret_cast<cudaStream_t>(stream);
+        // Programmatic dependent launch as well: every block waits for the
+        // preceding grid (griddepcontrol.wait) before it touches x or the
+        // partials, so all blocks are resident before the grid barrier.
+        cudaLaunchAttribute rattr[2] = {};
+        rattr[0].id = cudaLaunchAttributeCooperative;
+        rattr[0].val.cooperative = 1;
+        rattr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        rattr[1].val.programmaticStreamSerializationAllowed = 1;
+        rcfg.attrs = rattr;
+        rcfg.numAttrs = 2;
+        KZ_CHECK_CUDA(cudaLaunchKernelEx(&rcfg, quantize_resident_kernel, x, n, chunk, cap, partials, q, scale,
+                                         scale_f32, device_status_ptr()));
+        return KZ_OK;
     }
     const int g = (int)std::min<int64_t>(grid, (n + 16383) / 16384);
     cudaLaunchConfig_t cfg = {};

@@ -256,8 +256,9 @@ def dtensor_run(fn, output_placement, *dtensor_args):
 # --------------------------------------------------------- collectives
 
 def allreduce_partials_max(partials, group=None):
-    """Element-wise MAX of absmax partials across ranks, in place.  The two
-    grid-barrier words at the end of the buffer are left out."""
+    """Element-wise MAX of absmax partials across ranks, in place.  The
+    grid-barrier word and the reserved word at the end of the buffer are left
+    out."""
     words = partials[: _lib.KZ_PARTIALS_WORDS - 2]
     dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group)
     return partials
