@@ -12,8 +12,8 @@
 //   |t - x*r|     <= 2^-24 |x*r|   (+2^-149 if t is subnormal)
 // so |t - x/scale| < 127 * 2^-22.9 < 2^-16, and the double quotient differs
 // from x/scale by at most 128 * 2^-53.  Hence |t - fl64(x/scale)| < 2^-15.
-// Whenever t lies at least 2^-12 away from every half-integer
-// (|t - rint(t)| <= 1/2 - 2^-12), fl64(x/scale) lies in the same open interval
+// Whenever t lies at least 2^-15 away from every half-integer
+// (|t - rint(t)| <= 1/2 - 2^-15), fl64(x/scale) lies in the same open interval
 // (k - 1/2, k + 1/2) and rounds to the same k = rint(t).  The remaining
 // elements (about 1 in 2000 for smooth data) take the exact double division.
 // t - rint(t) is computed exactly (Sterbenz).  When 1/scale does not fit fp32
@@ -29,10 +29,11 @@
 // The vector form (pack4) folds the multiply into fused multiply-adds:
 // y = fl32(x*r + 1.5 * 2^23) gives k = y - 1.5 * 2^23, the integer nearest to
 // the exact product x*r, and d = fl32(x*r - k) its residual with one rounding
-// (|fl32(d) - d| <= 2^-25).  |x*r - x/scale| < 127 * 2^-24 < 2^-17, so
-// |fl64(x/scale) - k| <= |fl32(d)| + 2^-16 and |fl32(d)| <= 1/2 - 2^-12 again
-// proves k = rint(fl64(x/scale)).  Only the elements that fail the bound take
-// the exact division.
+// (|fl32(d) - d| <= 2^-25).  |x*r - x/scale| <= 127 (1 + 2^-52)(2^-24 + 2^-53
+// + 2^-77) < 2^-17.01, so |fl64(x/scale) - k| <= |fl32(d)| + 2^-25 + 2^-17.01
+// + 2^-46 < |fl32(d)| + 2^-16.9, and |fl32(d)| <= 1/2 - 2^-16 proves
+// k = rint(fl64(x/scale)).  Only the elements that fail the bound (about one in
+// 16000 for smooth data) take the exact division.
 #include <algorithm>
 #include <cfloat>
 #include <mutex>
@@ -41,7 +42,8 @@
 
 namespace kz {
 
-constexpr float kTieGuard = 0.5f - 1.0f / 4096.0f;
+constexpr float kTieGuard = 0.5f - 1.0f / 32768.0f;       // scalar form: |t - rint(t)| bound
+constexpr float kTieGuardFma = 0.5f - 1.0f / 65536.0f;    // fused-multiply-add form: |d| bound
 constexpr uint32_t kInfBits = 0x7F800000u;
 
 __device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
@@ -136,7 +138,7 @@ constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
 __device__ __forceinline__ uint32_t fma_code(float v, float rcp, bool* near) {
     const float y = __fmaf_rn(v, rcp, kRoundMagic);
     const float d = __fmaf_rn(v, rcp, -__fsub_rn(y, kRoundMagic));
-    *near = fabsf(d) > kTieGuard;
+    *near = fabsf(d) > kTieGuardFma;
     return __float_as_uint(y) & 0xFFu;
 }
 
@@ -150,6 +152,40 @@ __device__ __noinline__ uint32_t pack4_repair(float4 v, uint32_t w, double scale
         bool near = true;
         if (fast) fma_code(e[j], rcp, &near);
         if (near) w = (w & ~(0xFFu << (8 * j))) | ((uint32_t)(uint8_t)quant_exact(e[j], scale) << (8 * j));
+    }
+    return w;
+}
+
+// Fast-path word of four codes (little-endian) and the largest |residual| of
+// the four; residuals above kTieGuardFma mark elements for pack4_repair.
+__device__ __forceinline__ uint32_t pack4_fast(const float4& v, float rcp, float& dmax) {
+    const float y0 = __fmaf_rn(v.x, rcp, kRoundMagic), y1 = __fmaf_rn(v.y, rcp, kRoundMagic);
+    const float y2 = __fmaf_rn(v.z, rcp, kRoundMagic), y3 = __fmaf_rn(v.w, rcp, kRoundMagic);
+    const float d0 = __fmaf_rn(v.x, rcp, -__fsub_rn(y0, kRoundMagic));
+    const float d1 = __fmaf_rn(v.y, rcp, -__fsub_rn(y1, kRoundMagic));
+    const float d2 = __fmaf_rn(v.z, rcp, -__fsub_rn(y2, kRoundMagic));
+    const float d3 = __fmaf_rn(v.w, rcp, -__fsub_rn(y3, kRoundMagic));
+    const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
+    const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
+    dmax = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3)));
+    return __byte_perm(lo01, lo23, 0x5410);
+}
+
+// Sixteen codes from four float4: one tie check (one branch) for all of them,
+// so the four independent chains interleave.
+__device__ __forceinline__ uint4 pack16(const float4& a, const float4& b, const float4& c, const float4& d,
+                                        const ScaleInfo& si) {
+    float m0, m1, m2, m3;
+    uint4 w;
+    w.x = pack4_fast(a, si.rcp, m0);
+    w.y = pack4_fast(b, si.rcp, m1);
+    w.z = pack4_fast(c, si.rcp, m2);
+    w.w = pack4_fast(d, si.rcp, m3);
+    if (!si.fast || fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) > kTieGuardFma) {
+        if (!si.fast || m0 > kTieGuardFma) w.x = pack4_repair(a, w.x, si.scale, si.rcp, si.fast);
+        if (!si.fast || m1 > kTieGuardFma) w.y = pack4_repair(b, w.y, si.scale, si.rcp, si.fast);
+        if (!si.fast || m2 > kTieGuardFma) w.z = pack4_repair(c, w.z, si.scale, si.rcp, si.fast);
+        if (!si.fast || m3 > kTieGuardFma) w.w = pack4_repair(d, w.w, si.scale, si.rcp, si.fast);
     }
     return w;
 }
@@ -168,7 +204,7 @@ __device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) 
     const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
     const uint32_t w = __byte_perm(lo01, lo23, 0x5410);
     const float dm = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3)));
-    if (si.fast && dm <= kTieGuard) return w;
+    if (si.fast && dm <= kTieGuardFma) return w;
     return pack4_repair(v, w, si.scale, si.rcp, si.fast);
 }
 
@@ -225,12 +261,7 @@ __global__ void __launch_bounds__(256) quantize_partials_kernel(const float* __r
         for (int64_t i = tid; i < n16; i += nthreads) {
             const float4 a = __ldcs(xv + 4 * i), b = __ldcs(xv + 4 * i + 1);
             const float4 c = __ldcs(xv + 4 * i + 2), d = __ldcs(xv + 4 * i + 3);
-            uint4 o;
-            o.x = pack4(a, si);
-            o.y = pack4(b, si);
-            o.z = pack4(c, si);
-            o.w = pack4(d, si);
-            qv[i] = o;   // default policy: the int8 GEMM reads the codes next
+            qv[i] = pack16(a, b, c, d, si);   // default policy: the int8 GEMM reads the codes next
         }
         for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
     } else {
@@ -363,12 +394,7 @@ __global__ void __launch_bounds__(1024, 1) quantize_fused_kernel(const float* __
         for (int64_t i = tid; i < n16; i += nthreads) {
             const float4 a = __ldcs(xv + 4 * i), b = __ldcs(xv + 4 * i + 1);
             const float4 c = __ldcs(xv + 4 * i + 2), d = __ldcs(xv + 4 * i + 3);
-            uint4 o;
-            o.x = pack4(a, si);
-            o.y = pack4(b, si);
-            o.z = pack4(c, si);
-            o.w = pack4(d, si);
-            qv[i] = o;
+            qv[i] = pack16(a, b, c, d, si);
         }
         for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) q[j] = quant_one(x[j], si);
     } else {
@@ -444,7 +470,7 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
         }
     }
     if (!grid_barrier(partials, status) || !ok) return;
-    // phase 2: global absmax -> scale -> codes from shared memory
+    // phase 2: global absmax (one partial per thread) -> scale -> codes
     uint32_t bits = 0;
     for (uint32_t i = threadIdx.x; i < gridDim.x; i += blockDim.x) bits = max(bits, __ldcg(partials + 1 + i));
     bits = warp_max_u32(bits);
@@ -480,11 +506,11 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
     constexpr uint32_t B = kResidentBlock;
     uint32_t i = threadIdx.x;
     for (; i + 3 * B < res / 4; i += 4 * B) {
-        const float4 a0 = xs4[i], a1 = xs4[i + B], a2 = xs4[i + 2 * B], a3 = xs4[i + 3 * B];
-        qw[i] = pack4(a0, si);
-        qw[i + B] = pack4(a1, si);
-        qw[i + 2 * B] = pack4(a2, si);
-        qw[i + 3 * B] = pack4(a3, si);
+        const uint4 w = pack16(xs4[i], xs4[i + B], xs4[i + 2 * B], xs4[i + 3 * B], si);
+        qw[i] = w.x;
+        qw[i + B] = w.y;
+        qw[i + 2 * B] = w.z;
+        qw[i + 3 * B] = w.w;
     }
     for (; i < res / 4; i += B) qw[i] = pack4(xs4[i], si);
     uint32_t* qr = reinterpret_cast<uint32_t*>(q + r0);

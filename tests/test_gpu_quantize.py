@@ -119,6 +119,28 @@ def test_near_tie_stress_vs_oracle(kq):
         np.testing.assert_array_equal(q.cpu().numpy(), qo, err_msg=f"trial {trial} amax {amax}")
 
 
+@pytest.mark.parametrize("offset", [0, 1])
+def test_guard_band_stress_vs_oracle(kq, offset):
+    """Quotients at 2^-18 .. 2^-11 (in code units) from half-integers, on both
+    sides of the fast paths' tie guards (2^-16 for the fused multiply-add form,
+    2^-15 for the scalar form).  offset=1 makes the view unaligned, which takes
+    the scalar form."""
+    rs = np.random.RandomState(77 + offset)
+    for trial in range(4):
+        amax = float(np.float32(10.0 ** rs.uniform(-20, 20)))
+        scale = amax / 127.0
+        k = rs.randint(-127, 127, 300000)
+        delta = rs.choice([1.0, -1.0], k.size) * 2.0 ** rs.uniform(-18, -11, k.size)
+        v = ((k + 0.5 + delta) * scale).astype(np.float32)
+        v = np.clip(v, -np.float32(amax), np.float32(amax))
+        v[0] = np.float32(amax)
+        base = dev(np.concatenate([np.zeros(offset, np.float32), v]))
+        q, s64, _ = kq.quantize_tensor_device(base[offset:])
+        qo, so = ocpu.quantize_tensor(v)
+        assert float(s64.item()) == so
+        np.testing.assert_array_equal(q.cpu().numpy(), qo, err_msg=f"trial {trial} amax {amax}")
+
+
 def test_full_config2_activation_vs_oracle(kq):
     """BASELINE config 2 activations [2048, 4096] ~ N(0, 1), full size."""
     x = np.random.RandomState(1).standard_normal((2048, 4096)).astype(np.float32)
