@@ -143,9 +143,8 @@ __device__ __forceinline__ uint32_t fma_code(float v, float rcp, bool* near) {
 }
 
 // Exact-path repair of a packed word: only the near-tie bytes are recomputed,
-// so a warp with one such element pays for one division.  Kept out of line so
-// the hot loops do not carry its registers.
-__device__ __noinline__ uint32_t pack4_repair(float4 v, uint32_t w, double scale, float rcp, bool fast) {
+// so a warp with one such element pays for one division.
+__device__ __forceinline__ uint32_t pack4_repair(float4 v, uint32_t w, double scale, float rcp, bool fast) {
     const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -156,15 +155,40 @@ __device__ __noinline__ uint32_t pack4_repair(float4 v, uint32_t w, double scale
     return w;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: each lane rounds exactly like
+// the scalar instruction, so results are bit-identical).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // Fast-path word of four codes (little-endian) and the largest |residual| of
 // the four; residuals above kTieGuardFma mark elements for pack4_repair.
+// Per pair: y = fl(x*r + M), -k = M - y (exact), d = fl(x*r - k).
 __device__ __forceinline__ uint32_t pack4_fast(const float4& v, float rcp, float& dmax) {
-    const float y0 = __fmaf_rn(v.x, rcp, kRoundMagic), y1 = __fmaf_rn(v.y, rcp, kRoundMagic);
-    const float y2 = __fmaf_rn(v.z, rcp, kRoundMagic), y3 = __fmaf_rn(v.w, rcp, kRoundMagic);
-    const float d0 = __fmaf_rn(v.x, rcp, -__fsub_rn(y0, kRoundMagic));
-    const float d1 = __fmaf_rn(v.y, rcp, -__fsub_rn(y1, kRoundMagic));
-    const float d2 = __fmaf_rn(v.z, rcp, -__fsub_rn(y2, kRoundMagic));
-    const float d3 = __fmaf_rn(v.w, rcp, -__fsub_rn(y3, kRoundMagic));
+    const uint64_t R = pk2(rcp, rcp), Mg = pk2(kRoundMagic, kRoundMagic);
+    const uint64_t v01 = pk2(v.x, v.y), v23 = pk2(v.z, v.w);
+    const uint64_t y01 = fma2(v01, R, Mg), y23 = fma2(v23, R, Mg);
+    const uint64_t d01 = fma2(v01, R, sub2(Mg, y01)), d23 = fma2(v23, R, sub2(Mg, y23));
+    float y0, y1, y2, y3, d0, d1, d2, d3;
+    upk2(y01, y0, y1);
+    upk2(y23, y2, y3);
+    upk2(d01, d0, d1);
+    upk2(d23, d2, d3);
     const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
     const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
     dmax = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3)));
@@ -194,16 +218,8 @@ __device__ __forceinline__ uint4 pack16(const float4& a, const float4& b, const 
 // element and one tie check per four; a word with a near-tie element is
 // repaired per element.
 __device__ __forceinline__ uint32_t pack4(const float4& v, const ScaleInfo& si) {
-    const float y0 = __fmaf_rn(v.x, si.rcp, kRoundMagic), y1 = __fmaf_rn(v.y, si.rcp, kRoundMagic);
-    const float y2 = __fmaf_rn(v.z, si.rcp, kRoundMagic), y3 = __fmaf_rn(v.w, si.rcp, kRoundMagic);
-    const float d0 = __fmaf_rn(v.x, si.rcp, -__fsub_rn(y0, kRoundMagic));
-    const float d1 = __fmaf_rn(v.y, si.rcp, -__fsub_rn(y1, kRoundMagic));
-    const float d2 = __fmaf_rn(v.z, si.rcp, -__fsub_rn(y2, kRoundMagic));
-    const float d3 = __fmaf_rn(v.w, si.rcp, -__fsub_rn(y3, kRoundMagic));
-    const uint32_t lo01 = __byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040);
-    const uint32_t lo23 = __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040);
-    const uint32_t w = __byte_perm(lo01, lo23, 0x5410);
-    const float dm = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3)));
+    float dm;
+    const uint32_t w = pack4_fast(v, si.rcp, dm);
     if (si.fast && dm <= kTieGuardFma) return w;
     return pack4_repair(v, w, si.scale, si.rcp, si.fast);
 }
