@@ -52,8 +52,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--workload", choices=["linear", "stack"], default="linear",
-                    help="linear: BASELINE config 2 (default); stack: config 5, column-sharded 4-layer stack")
+    ap.add_argument("--workload", choices=["linear", "stack", "transformer", "sweep", "mlp"], default="linear",
+                    help="linear: config 2 (default); stack: config 5, column-sharded 4-layer stack; "
+                         "transformer: config 3 decoder; sweep: config 4 square GEMMs; mlp: config 1")
     return ap.parse_args()
 
 
@@ -236,8 +237,9 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if args.workload == "stack":
-        run_stack(args, rank, world, local_rank, dev)
+    if args.workload != "linear":
+        {"stack": run_stack, "transformer": run_transformer, "sweep": run_sweep, "mlp": run_mlp}[args.workload](
+            args, rank, world, local_rank, dev)
         return
 
     import kansaiml_b200 as kz
@@ -505,6 +507,166 @@ def run_stack(args, rank, world, local_rank, dev):
                      "peak_source": f"{world} x 2 x bf16_tflops ({bf16:.1f}, {peak_src})"},
         "gpu_launches": (1 + 2 * STACK_L - 1) * K,
         "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
+
+
+
+def _graph_of(fn, reps, dev):
+    """A CUDA graph of `reps` calls of fn (warmed up eagerly first)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(reps):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def _time_graph(g, reps_per_graph, steps, warmup, local_rank, dev):
+    """Replays g until `steps` calls ran; returns (ms per call, clocks)."""
+    import torch
+    for _ in range(max(1, -(-warmup // reps_per_graph))):
+        g.replay()
+    torch.cuda.synchronize()
+    n = max(1, -(-steps // reps_per_graph))
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for _ in range(n):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    return start.elapsed_time(end) / (n * reps_per_graph), n * reps_per_graph, clk.summary()
+
+
+def run_transformer(args, rank, world, local_rank, dev):
+    """int8 2-layer decoder (d_model 256, 4 heads, FFN 1024
+    GELU, vocab 65, context 256, batch 32 = 8192 tokens), per-channel int8
+    weights, per-tensor int8 activations, fp32 LayerNorm / attention / softmax.
+    One step = one forward of the batch, captured in a CUDA graph."""
+    import torch
+    from kansaiml_b200 import workloads
+
+    model = workloads.Decoder(seed=3, device=dev)
+    ids = workloads.config3_ids(seed=4, device=dev)
+    reps = 4
+    g = _graph_of(lambda: model(ids), reps, dev)
+    ms, steps, clocks = _time_graph(g, reps, args.steps, max(args.warmup, 3), local_rank, dev)
+    if rank != 0:
+        return
+    tokens = ids.numel()
+    ops = 2 * 2 * tokens * (4 * 256 * 256 + 2 * 256 * 1024) + 2 * tokens * 256 * 65
+    line = {
+        "metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "config3: int8 2-layer decoder d256 h4 ff1024 vocab65 ctx256, batch 32",
+                   "global_batch": tokens, "seq_len": 256, "parallelism": "single GPU",
+                   "launch": f"CUDA graphs of {reps} forwards replayed back to back"},
+        "int8_ops_per_step": ops, "int8_tops": ops / (ms / 1e3) / 1e12,
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+SWEEP_N = (1024, 2048, 4096, 8192, 16384)
+
+
+def run_sweep(args, rank, world, local_rank, dev):
+    """square int8 GEMMs M = N = K in SWEEP_N, operands
+    ~ U{-127..127}, per-row x per-column fp32 scales ~ U[1e-3, 1e-2] fused into
+    the epilogue (fp32 out), and the int32-output form.  Sets of operands
+    rotate so that each size's working set exceeds L2."""
+    import torch
+    from kansaiml_b200 import _lib
+
+    lib = _lib.load()
+    hbm_gbs, bf16, _, peak_src = peaks()
+    peak = 2.0 * bf16
+    rows, clocks = [], None
+    for n in SWEEP_N:
+        nsets = max(1, -(-(256 << 20) // (6 * n * n)))
+        g = torch.Generator(device=dev)
+        g.manual_seed(n)
+        sets = []
+        for _ in range(nsets):
+            a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            rs = torch.rand(n, device=dev, generator=g) * 9e-3 + 1e-3
+            cs = torch.rand(n, device=dev, generator=g) * 9e-3 + 1e-3
+            sets.append((a, b, rs, cs, torch.empty((n, n), dtype=torch.float32, device=dev)))
+        res = {"n": n, "sets": nsets}
+        for form in ("fp32_epilogue", "int32"):
+            def call():
+                sh = torch.cuda.current_stream(dev).cuda_stream
+                for a, b, rs, cs, y in sets:
+                    if form == "int32":
+                        st = lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, None, 0, None, 0, None, 0, None,
+                                            y.data_ptr(), n, None, sh)
+                    else:
+                        st = lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, rs.data_ptr(), 1, cs.data_ptr(), 1,
+                                            None, 0, y.data_ptr(), None, n, None, sh)
+                    if st:
+                        raise RuntimeError(_lib.last_error())
+            reps = max(1, 16 // nsets) if n <= 4096 else 1
+            gr = _graph_of(call, reps, dev)
+            steps = max(4, min(args.steps, int(2e13 / (2.0 * n ** 3))))
+            ms, done, clocks = _time_graph(gr, reps * nsets, steps, max(args.warmup, 3), local_rank, dev)
+            tops = 2.0 * n ** 3 / (ms / 1e3) / 1e12
+            res[form] = {"us": ms * 1e3, "tops": tops, "frac": tops / peak, "launches": done}
+            del gr
+        rows.append(res)
+        del sets
+        torch.cuda.empty_cache()
+    head = next(r for r in rows if r["n"] == 8192)
+    line = {
+        "metric": METRIC, "value": head["fp32_epilogue"]["tops"], "unit": "TOP/s", "n_gpus": 1,
+        "steps": head["fp32_epilogue"]["launches"], "warmup": max(args.warmup, 3),
+        "ms_per_step": head["fp32_epilogue"]["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "config4: square int8 GEMM sweep, per-row x per-column fp32 scale epilogue; "
+                               "value = M=N=K=8192", "global_batch": None, "seq_len": None,
+                   "parallelism": "single GPU", "l2": "operand sets rotate so each size's working set exceeds L2"},
+        "sweep": rows,
+        "roofline": {"kernel": "gemm_i8_kernel", "bound": "tensor", "peak": peak, "unit": "TOP/s",
+                     "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src})"},
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+def run_mlp(args, rank, world, local_rank, dev):
+    """int8 MLP 784 -> 256 -> 10 (ReLU), batch 64, per-tensor
+    weights and fp32 activations: the reference's own semantics
+    (qlinear = x @ dequantize(W) + b), bit-identical outputs.  One step = one
+    forward, captured in a CUDA graph."""
+    import torch
+    import kansaiml_b200 as kz
+    from kansaiml_b200 import nn
+    from kansaiml_b200.quantize import QLinear
+
+    l1, l2 = nn.Linear(784, 256, seed=1, device=dev), nn.Linear(256, 10, seed=2, device=dev)
+    model = nn.Sequential(QLinear(l1), nn.ReLU(), QLinear(l2))
+    x = kz.from_numpy(np.random.RandomState(0).uniform(0, 1, (64, 784)).astype(np.float32), device=dev)
+    reps = 16
+    g = _graph_of(lambda: model(x), reps, dev)
+    ms, steps, clocks = _time_graph(g, reps, args.steps, max(args.warmup, 3), local_rank, dev)
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": 64 / (ms / 1e3), "unit": "rows/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (W8A32, reference semantics)", "data": "synthetic",
+        "config": {"workload": "config1: int8 MLP 784-256-10 ReLU, batch 64, per-tensor weights, fp32 activations",
+                   "global_batch": 64, "seq_len": None, "parallelism": "single GPU",
+                   "launch": f"CUDA graphs of {reps} forwards"},
+        "us_per_forward": ms * 1e3,
+        "clocks": clocks,
     }
     print(json.dumps(line))
 
