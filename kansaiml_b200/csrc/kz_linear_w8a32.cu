@@ -90,6 +90,69 @@ __global__ void __launch_bounds__(256) qlinear_w8a32_kernel(const float* __restr
     }
 }
 
+// Small-M form: one thread per output, so M x N independent k-ordered chains
+// run at once (the 64 x 64 tiles above give a 64-row batch only N / 64
+// blocks).  A block is 4 rows (one warp each) x 32 columns (one lane each);
+// the weight is staged 32 k x 32 n at a time, dequantized through the table,
+// double-buffered in shared memory with the next chunk's codes and x values
+// prefetched into registers; x[m, k] reaches every lane of the row's warp by
+// shuffle.  Same operations in the same order as the tiled kernel.
+constexpr int kRowsR = 4, kColsR = 32, kChunkR = 32;
+
+__global__ void __launch_bounds__(128) qlinear_w8a32_rows_kernel(const float* __restrict__ x, int64_t M, int64_t K,
+                                                                 const int8_t* __restrict__ q, double scale,
+                                                                 const float* __restrict__ bias, int64_t N, int act,
+                                                                 float* __restrict__ out) {
+    __shared__ float table[256];
+    __shared__ float ws[2][kChunkR][kColsR + 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < 256; i += 128)
+        table[i] = i < 255 ? __double2float_rn((double)(i - 127) * scale) : __double2float_rn(-128.0 * scale);
+    const int64_t m = blockIdx.y * (int64_t)kRowsR + warp;
+    const int64_t n0 = blockIdx.x * (int64_t)kColsR;
+    const bool row_ok = m < M;
+    // staging map: thread t owns chunk row kk = t / 4 and columns 8 (t % 4) .. + 7
+    const int skk = tid >> 2, sc0 = (tid & 3) * 8;
+    int8_t code[8];
+    float xr = 0.0f;
+    auto fetch = [&](int64_t k0) {
+        const int64_t k = k0 + skk;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t n = n0 + sc0 + j;
+            code[j] = (k < K && n < N) ? __ldg(q + k * N + n) : (int8_t)0;
+        }
+        xr = (row_ok && k0 + lane < K) ? __ldg(x + m * K + k0 + lane) : 0.0f;
+    };
+    fetch(0);
+    __syncthreads();   // table ready
+    float acc = 0.0f;
+    int buf = 0;
+    for (int64_t k0 = 0; k0 < K; k0 += kChunkR) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ws[buf][skk][sc0 + j] = table[((int)code[j] + 127) & 255];
+        const float xc = xr;
+        if (k0 + kChunkR < K) fetch(k0 + kChunkR);
+        __syncthreads();
+        const int kend = (int)min((int64_t)kChunkR, K - k0);
+        if (kend == kChunkR) {
+#pragma unroll
+            for (int kk = 0; kk < kChunkR; ++kk)   // k order preserved
+                acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, xc, kk), ws[buf][kk][lane]));
+        } else {
+            for (int kk = 0; kk < kend; ++kk)
+                acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, xc, kk), ws[buf][kk][lane]));
+        }
+        buf ^= 1;
+    }
+    const int64_t n = n0 + lane;
+    if (row_ok && n < N) {
+        float v = acc;
+        if (bias) v = __fadd_rn(v, bias[n]);
+        out[m * N + n] = act_apply(v, act);
+    }
+}
+
 }  // namespace kz
 
 using namespace kz;
@@ -101,10 +164,19 @@ extern "C" int kz_qlinear_w8a32_f32(const float* x, int64_t M, int64_t K, const 
     if (M == 0 || N == 0) return KZ_OK;
     KZ_REQUIRE(out != nullptr, "kz_qlinear_w8a32_f32: out is NULL");
     KZ_REQUIRE(K == 0 || (x && q), "kz_qlinear_w8a32_f32: x or q is NULL");
-    KZ_REQUIRE((M + kBM - 1) / kBM < 65536, "kz_qlinear_w8a32_f32: M too large");
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // Few 64 x 64 tiles (small batches) leave most SMs idle: one thread per
+    // output instead.  Both kernels round identically.
+    const int64_t tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+    if (tiles < 2 * (int64_t)sm_count()) {
+        KZ_REQUIRE((M + kRowsR - 1) / kRowsR < 65536, "kz_qlinear_w8a32_f32: M too large");
+        dim3 grid((unsigned)((N + kColsR - 1) / kColsR), (unsigned)((M + kRowsR - 1) / kRowsR));
+        qlinear_w8a32_rows_kernel<<<grid, 128, 0, s>>>(x, M, K, q, scale, bias, N, act, out);
+        return launch_status("qlinear_w8a32_rows_kernel");
+    }
+    KZ_REQUIRE((M + kBM - 1) / kBM < 65536, "kz_qlinear_w8a32_f32: M too large");
     dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
     qlinear_w8a32_kernel<<<grid, 256, 0, s>>>(x, M, K, q, scale, bias, N, act, out);
     return launch_status("qlinear_w8a32_kernel");

@@ -67,6 +67,25 @@ def test_mlp_config1_bit_exact(k):
     assert h.tobytes() == g["h"].tobytes()
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 33, 10), (3, 784, 65), (64, 784, 256), (64, 256, 10), (300, 200, 300),
+                                   (2048, 512, 1024), (129, 31, 1)])
+def test_w8a32_shapes_vs_oracle(k, M, K, N):
+    """Both W8A32 kernels (one thread per output for small batches, 64 x 64
+    tiles for large ones) against the oracle's k-ordered fp32 loop, bit-exact,
+    on ragged K and N."""
+    kz, nn, kq = k
+    rs = np.random.RandomState(M * 7 + K + N)
+    x = rs.standard_normal((M, K)).astype(np.float32)
+    w = (rs.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
+    bias = rs.standard_normal(N).astype(np.float32)
+    qw = kq.QTensor.from_tensor(dev(w))
+    q = qw.codes.cpu().numpy().reshape(K, N)
+    for act in (0, 1):
+        y = kq.qlinear(dev(x), qw, dev(bias), act=[None, "relu"][act]).numpy()
+        yo = ocpu.qlinear_w8a32(x, q, qw.scale, bias, act)
+        assert y.tobytes() == yo.tobytes(), (M, K, N, act)
+
+
 def test_xor_quantized_predictions(k):
     """tests/test_quantize.py:81-125: the trained XOR model, quantized."""
     kz, nn, kq = k
