@@ -93,13 +93,25 @@ int kz_absmax_f32(const float* x, int64_t n, uint32_t* partials, kz_stream_t str
 int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials, int8_t* q,
                              double* scale, float* scale_f32, kz_stream_t stream);
 
-/* quantize_symmetric (quantize.py:50-70) on the device.  Large tensors run as
- * ONE cooperative launch (absmax, a bounded grid barrier in the last two words
- * of `partials`, quantize while x is still in L2); small ones as
- * kz_absmax_f32 + kz_quantize_partials_f32.  `partials` is caller scratch,
- * zero-filled before its first use (see KZ_PARTIALS_WORDS). */
+/* quantize_symmetric (quantize.py:50-70) on the device.  Tensors of 65536
+ * elements or more run as ONE cooperative launch (absmax, a bounded grid
+ * barrier in the second-to-last word of `partials`, quantize; with x and q
+ * 16-byte aligned each block keeps its slice of x in shared memory, so x is
+ * read from HBM once); smaller ones as kz_absmax_f32 + kz_quantize_partials_f32.
+ * `partials` is caller scratch, zero-filled before its first use (see
+ * KZ_PARTIALS_WORDS). */
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
                            uint32_t* partials, kz_stream_t stream);
+
+/* LayerNorm over the last axis of x[M, D] (nn.py:308-331: mean, biased
+ * variance, eps; y = (x - mean) / sqrt(var + eps) * gamma + beta, gamma/beta
+ * may be NULL for 1/0), writing y[M, D] and the absmax partials of y in the
+ * KZ_PARTIALS_WORDS format, so kz_quantize_partials_f32 quantizes y per tensor
+ * without another pass over it: the prologue of a quantized Linear that
+ * follows a LayerNorm.  No reference counterpart (the reference runs
+ * LayerNorm and quantize_symmetric separately).  fp32 throughout. */
+int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
+                              float* y, uint32_t* partials, kz_stream_t stream);
 
 /* Per-output-channel quantize of a reference-layout weight w[K, N] (row-major,
  * nn.py:74-81: [in_features, out_features]); channel n is column n.  Writes

@@ -534,6 +534,60 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
     for (int64_t j = r0 + 4 * rem4 + threadIdx.x; j < e1; j += blockDim.x) q[j] = quant_one(x[j], si);
 }
 
+// ------------------------------------------- LayerNorm with absmax partials
+
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// LayerNorm over the last axis (nn.py:308-331: mean, biased variance, eps;
+// y = (x - mean) / sqrt(var + eps) * gamma + beta), one warp per row, writing
+// y and the absmax partials of y (block b -> partials[1 + b]) so that
+// kz_quantize_partials_f32 can quantize y per tensor without another pass.
+__global__ void __launch_bounds__(256) layernorm_partials_kernel(const float* __restrict__ x, int64_t M, int64_t D,
+                                                                 const float* __restrict__ gamma,
+                                                                 const float* __restrict__ beta, float eps,
+                                                                 float* __restrict__ y,
+                                                                 uint32_t* __restrict__ partials) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float inv_d = __frcp_rn((float)D);
+    uint32_t m = 0;
+    for (int64_t r = blockIdx.x * 8 + warp; r < M; r += (int64_t)gridDim.x * 8) {
+        const float* xr = x + r * D;
+        float s = 0.0f;
+        for (int64_t j = lane; j < D; j += 32) s = __fadd_rn(s, xr[j]);
+        const float mean = __fmul_rn(warp_sum_f32(s), inv_d);
+        float v = 0.0f;
+        for (int64_t j = lane; j < D; j += 32) {
+            const float c = __fsub_rn(xr[j], mean);
+            v = __fadd_rn(v, __fmul_rn(c, c));
+        }
+        const float den = __fsqrt_rn(__fadd_rn(__fmul_rn(warp_sum_f32(v), inv_d), eps));
+        float* yr = y + r * D;
+        for (int64_t j = lane; j < D; j += 32) {
+            float o = __fdiv_rn(__fsub_rn(xr[j], mean), den);
+            if (gamma) o = __fmul_rn(o, gamma[j]);
+            if (beta) o = __fadd_rn(o, beta[j]);
+            yr[j] = o;
+            m = max(m, abs_bits(o));
+        }
+    }
+    m = warp_max_u32(m);
+    __shared__ uint32_t red[8];
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t v = 0;
+        for (int w = 0; w < 8; ++w) v = max(v, red[w]);
+        partials[1 + blockIdx.x] = v;
+        if (blockIdx.x == 0) partials[0] = gridDim.x;
+    }
+}
+
 // ------------------------------------------------------ per-column (weights)
 
 // Column absmax partials: partial[r][n] = max over rows of split r of |w[k][n]|.
@@ -749,6 +803,21 @@ static int fused_grid(int dev) {
     if (g > kFusedMaxBlocks) g = kFusedMaxBlocks;
     if (dev >= 0 && dev < 64) cached[dev] = g;
     return g;
+}
+
+int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
+                              float* y, uint32_t* partials, kz_stream_t stream) {
+    KZ_REQUIRE(M >= 0 && D > 0, "kz_layernorm_partials_f32: need M >= 0 and D > 0");
+    KZ_REQUIRE(partials, "kz_layernorm_partials_f32: partials is NULL");
+    KZ_REQUIRE(M == 0 || (x && y), "kz_layernorm_partials_f32: x or y is NULL");
+    int st = check_device();
+    if (st) return st;
+    const int64_t cap = std::min<int64_t>(4 * (int64_t)sm_count(), kFusedMaxBlocks);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, cap));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    KZ_CHECK_CUDA(launch_pdl(layernorm_partials_kernel, dim3(grid), dim3(256), 0, s, x, M, D, gamma, beta, eps, y,
+                             partials));
+    return KZ_OK;
 }
 
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,

@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from .quantize import QLinear
+from .quantize import QActivation, QLinear, partials_buffer
 from .tensor import Tensor, as_tensor, from_flat, ones, randn, zeros
 
 
@@ -125,7 +125,11 @@ class MultiHeadAttention(Module):
     """nn.py:334-427: raw [d, d] projections w_q, w_k, w_v, w_o (no bias),
     scaled dot-product attention with an optional additive mask, fp32.
     ``quantize(per_channel=True)`` swaps the four projections for int8 QLinear
-    layers (bias-free); attention scores and softmax stay fp32."""
+    layers (bias-free); attention scores and softmax stay fp32.  With a
+    per-channel weight, self-attention (query, key and value the same input)
+    runs the three input projections as ONE int8 GEMM over the concatenated
+    [d, 3d] weight: per-channel codes and scales are per column, so each
+    column is the same as its separate projection's, bit for bit."""
 
     def __init__(self, d_model, num_heads, seed=0, device=None):
         if d_model % num_heads:
@@ -137,6 +141,7 @@ class MultiHeadAttention(Module):
         self.w_v = randn([d_model, d_model], std=std, seed=seed + 2, device=device)
         self.w_o = randn([d_model, d_model], std=std, seed=seed + 3, device=device)
         self.q_proj = None
+        self.qkv = None
 
     def quantize(self, per_channel=True, activations=None):
         class _W:  # a Linear-shaped view of a bias-free projection
@@ -144,6 +149,9 @@ class MultiHeadAttention(Module):
                 self.weight, self.bias = w, None
         self.q_proj = [QLinear(_W(w), per_channel=per_channel, activations=activations)
                        for w in (self.w_q, self.w_k, self.w_v, self.w_o)]
+        if per_channel and activations in (None, "int8"):
+            qkv = torch.cat([self.w_q.data, self.w_k.data, self.w_v.data], dim=1)
+            self.qkv = QLinear(_W(Tensor(qkv)), per_channel=True, activations=activations)
         return self
 
     def _proj(self, x, i, w):
@@ -152,6 +160,10 @@ class MultiHeadAttention(Module):
         return x.matmul(w)
 
     def forward(self, query, key, value, mask=None):
+        if self.qkv is not None and query is key and key is value:
+            return self._self_attention(query, mask)
+        if isinstance(query, QActivation):
+            raise ValueError("a pre-quantized input needs the fused self-attention path")
         q_in, k_in, v_in = as_tensor(query), as_tensor(key), as_tensor(value)
         b, sq, _ = q_in.shape
         _, sk, _ = k_in.shape
@@ -165,6 +177,19 @@ class MultiHeadAttention(Module):
         att = torch.matmul(torch.softmax(scores, 3), v)
         merged = Tensor(att.transpose(1, 2).reshape(b, sq, self.d_model).contiguous())
         return self._proj(merged, 3, self.w_o)
+
+
+    def _self_attention(self, x, mask):
+        """One int8 GEMM for q, k and v, fp32 scaled dot-product attention
+        (softmax(q k^T / sqrt(d_k) + mask) v in one kernel), int8 output
+        projection."""
+        b, s, _ = x.shape
+        h, dk = self.num_heads, self.d_k
+        qkv = self.qkv(x).data.reshape(b, s, 3, h, dk).permute(2, 0, 3, 1, 4)
+        m = as_tensor(mask).data if mask is not None else None
+        att = torch.nn.functional.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=m)
+        merged = Tensor(att.transpose(1, 2).reshape(b, s, self.d_model))
+        return self.q_proj[3](merged)
 
 
 class TransformerBlock(Module):
@@ -187,6 +212,8 @@ class TransformerBlock(Module):
 
     def forward(self, x, mask=None):
         x = as_tensor(x)
+        if isinstance(self.fc1, QLinear) and self.attn.qkv is not None:
+            return self._forward_w8a8(x, mask)
         normed = self.ln1(x)
         x = x.add(self.attn(normed, normed, normed, mask=mask))
         h = self.ln2(x)
@@ -195,6 +222,19 @@ class TransformerBlock(Module):
         else:
             h = self.gelu(self.fc1(h))
         return x.add(self.fc2(h))
+
+    def _forward_w8a8(self, x, mask):
+        """The same block with every activation quantized where it is made:
+        LayerNorm -> quantize is one LayerNorm kernel (with the absmax) plus
+        one quantize pass; fc1's GEMM epilogue (bias + GELU) also emits the
+        absmax of its output, so fc2's input is quantized in one pass."""
+        ln1, ln2 = self.ln1, self.ln2
+        qa = QActivation.layernorm(x, ln1.weight, ln1.bias, ln1.eps)
+        x = x.add(self.attn(qa, qa, qa, mask=mask))
+        qb = QActivation.layernorm(x, ln2.weight, ln2.bias, ln2.eps)
+        partials = partials_buffer(x.data.device)
+        h = self.fc1(qb, act="gelu", out_partials=partials)
+        return x.add(self.fc2(QActivation.from_partials(h, partials)))
 
 
 def causal_mask(seq, device=None):

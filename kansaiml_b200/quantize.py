@@ -90,6 +90,23 @@ def quantize_partials_device(x, partials):
     return q, s64, s32
 
 
+def layernorm_partials_device(x, weight=None, bias=None, eps=1e-5, partials=None):
+    """LayerNorm over the last axis of a contiguous fp32 CUDA tensor, plus the
+    absmax partials of the result (kz_layernorm_partials_f32).
+    Returns (y, partials)."""
+    dev = x.device
+    D = x.shape[-1]
+    M = x.numel() // D
+    if partials is None:
+        partials = partials_buffer(dev)
+    y = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    w = _dev_tensor(weight, "layernorm weight") if weight is not None else None
+    b = _dev_tensor(bias, "layernorm bias") if bias is not None else None
+    _lib.call("kz_layernorm_partials_f32", ptr(x), M, D, ptr(w), ptr(b), float(eps), ptr(y), ptr(partials),
+              stream_handle(dev))
+    return y, partials
+
+
 def absmax_partials_device(x, partials=None):
     dev = x.device
     if partials is None:
@@ -157,6 +174,45 @@ def device_status(device=None, clear=True):
 
 
 # ------------------------------------------------------------ QTensor
+
+class QActivation:
+    """An activation quantized per tensor for the W8A8 path: int8 codes in the
+    activation's own layout and its scale (float64 and float32, one element
+    each, on the device).  ``qlinear`` accepts it in place of an fp32 input and
+    skips its own quantize step, which lets the producer of the activation
+    supply the absmax: a LayerNorm (``layernorm``) or the epilogue of the
+    previous int8 GEMM (``from_partials``)."""
+
+    __slots__ = ("codes", "scale64", "scale_f32")
+
+    def __init__(self, codes, scale64, scale_f32):
+        self.codes, self.scale64, self.scale_f32 = codes, scale64, scale_f32
+
+    @property
+    def shape(self):
+        return list(self.codes.shape)
+
+    @property
+    def scale(self):
+        return float(self.scale64.item())
+
+    @classmethod
+    def from_tensor(cls, x):
+        return cls(*quantize_tensor_device(_dev_tensor(x, "QActivation")))
+
+    @classmethod
+    def from_partials(cls, x, partials):
+        """x's codes from absmax partials that describe exactly x (e.g. the
+        partials the GEMM that produced x wrote): one pass over x."""
+        return cls(*quantize_partials_device(_dev_tensor(x, "QActivation"), partials))
+
+    @classmethod
+    def layernorm(cls, x, weight=None, bias=None, eps=1e-5):
+        """LayerNorm (nn.py:308-331) of x, quantized per tensor: the LayerNorm
+        kernel emits the absmax partials, so the quantize is a single pass."""
+        y, partials = layernorm_partials_device(_dev_tensor(x, "QActivation.layernorm"), weight, bias, eps)
+        return cls(*quantize_partials_device(y, partials))
+
 
 class QTensor:
     """An int8 tensor plus its scale(s) and shape (quantize.py:80-112).
@@ -322,7 +378,7 @@ def _flatten_rows(x):
     return t.reshape(-1, t.shape[-1]), lead
 
 
-def qlinear(x, qweight: QTensor, bias=None, activations=None, act=None) -> Tensor:
+def qlinear(x, qweight: QTensor, bias=None, activations=None, act=None, out_partials=None) -> Tensor:
     """quantize.py:115-122: a Linear forward with an int8 weight.
 
     activations="fp32" (default for a per-tensor weight): the reference's
@@ -331,9 +387,26 @@ def qlinear(x, qweight: QTensor, bias=None, activations=None, act=None) -> Tenso
     weight): W8A8 on the tensor cores with the epilogue fused.
     act: optional "relu" / "gelu" applied in the same kernel (the value is the
     same as applying nn.ReLU / nn.GELU afterwards).
+    x may be a QActivation (already quantized per tensor): the W8A8 GEMM then
+    consumes its codes directly.  out_partials (W8A8 only): a KZ_PARTIALS_WORDS
+    buffer that receives the absmax partials of the output, for
+    QActivation.from_partials.
     """
+    if isinstance(x, QActivation):
+        codes = x.codes.reshape(-1, x.codes.shape[-1])
+        M, K = codes.shape
+        if len(qweight.shape) != 2 or qweight.shape[0] != K:
+            raise RuntimeError("matmul: incompatible shapes")
+        if K % 16:
+            raise ValueError(f"W8A8 qlinear needs in_features % 16 == 0 (got {K})")
+        b = _dev_tensor(bias, "qlinear bias").reshape(-1) if bias is not None else None
+        out, _ = gemm_i8_device(codes, qweight.kmajor(), row_scale=x.scale_f32, col_scale=qweight.scale_f32, bias=b,
+                                act=act, partials=out_partials)
+        return Tensor(out.reshape(x.shape[:-1] + [qweight.shape[1]]))
     if activations is None:
         activations = "fp32" if qweight.granularity == "tensor" else "int8"
+    if out_partials is not None and activations == "fp32":
+        raise ValueError("out_partials needs the W8A8 path")
     xt = _dev_tensor(x, "qlinear")
     x2, lead = _flatten_rows(xt)
     x2 = x2.contiguous()
@@ -360,7 +433,8 @@ def qlinear(x, qweight: QTensor, bias=None, activations=None, act=None) -> Tenso
             xq, _, xs32 = quantize_tensor_device(x2)
         else:
             xq, _, xs32 = quantize_rows_device(x2)
-        out, _ = gemm_i8_device(xq, qweight.kmajor(), row_scale=xs32, col_scale=qweight.scale_f32, bias=b, act=act)
+        out, _ = gemm_i8_device(xq, qweight.kmajor(), row_scale=xs32, col_scale=qweight.scale_f32, bias=b, act=act,
+                                partials=out_partials)
     else:
         raise ValueError(f"unknown activations mode {activations!r}")
     return Tensor(out.reshape(lead + [N]))
@@ -381,8 +455,8 @@ class QLinear:
         self.bias = as_tensor(linear.bias, device=self.qweight.device) if linear.bias is not None else None
         self.activations = activations
 
-    def __call__(self, x, act=None):
-        return qlinear(x, self.qweight, self.bias, activations=self.activations, act=act)
+    def __call__(self, x, act=None, out_partials=None):
+        return qlinear(x, self.qweight, self.bias, activations=self.activations, act=act, out_partials=out_partials)
 
     def forward(self, x, act=None):
         return self(x, act)

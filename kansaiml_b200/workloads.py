@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from . import nn
-from .quantize import QLinear
+from .quantize import QActivation, QLinear
 from .tensor import Tensor, from_numpy
 
 
@@ -59,7 +59,8 @@ class Decoder(nn.Module):
         mask = self.mask if s == self.ctx else Tensor(self.mask.data[:, :, :s, :s])
         for blk in self.blocks:
             x = blk(x, mask=mask)
-        return self.head(self.ln(x))
+        ln = self.ln
+        return self.head(QActivation.layernorm(x, ln.weight, ln.bias, ln.eps))
 
 
 def config3_ids(batch=32, ctx=256, vocab=65, seed=0, device="cuda"):

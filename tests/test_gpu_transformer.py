@@ -4,9 +4,12 @@ Linear per-channel int8 with per-tensor int8 activations; LayerNorm, attention
 and softmax fp32.
 
 1. Layer by layer: every quantized Linear call inside the forward is redone
-   by the oracle from the fp32 input that layer received on the device.  The
-   activation codes and scale, the int32 accumulators (sampled rows) and the
-   fp32 outputs must be bit-exact (GELU layers: 1e-5 relative, CUDA erff).
+   by the oracle from the input that layer received on the device (fp32, or
+   int8 codes + scale when the producer quantized it).  The activation codes
+   and scale, the int32 accumulators (sampled rows) and the fp32 outputs must
+   be bit-exact (GELU layers: 1e-5 relative, CUDA erff).  fc2's input codes,
+   quantized from the absmax partials of fc1's epilogue, must equal the
+   oracle's per-tensor quantize of fc1's output exactly.
 2. End to end: the logits are compared with an fp32 numpy forward that runs
    every Linear through the oracle.  LayerNorm and softmax reduce in a
    different order in numpy and torch, so an activation lying on a rounding
@@ -39,19 +42,32 @@ def test_layerwise_bit_exact(model_and_ids, monkeypatch):
     calls = []
     inner = kq.qlinear
 
-    def recording(x, qweight, bias=None, activations=None, act=None):
-        out = inner(x, qweight, bias, activations=activations, act=act)
-        calls.append((x.numpy().reshape(-1, qweight.shape[0]), qweight, bias, act, out.numpy()))
+    def recording(x, qweight, bias=None, activations=None, act=None, out_partials=None):
+        out = inner(x, qweight, bias, activations=activations, act=act, out_partials=out_partials)
+        K = qweight.shape[0]
+        if isinstance(x, kq.QActivation):
+            xin = (x.codes.cpu().numpy().reshape(-1, K), x.scale)
+        else:
+            xin = x.numpy().reshape(-1, K)
+        calls.append((xin, qweight, bias, act, out.numpy()))
         return out
 
     monkeypatch.setattr(kq, "qlinear", recording)
     model(ids)
-    assert len(calls) == 2 * 6 + 1
+    # per block: fused qkv, output projection, fc1, fc2; then the head
+    assert len(calls) == 2 * 4 + 1
     rows = np.random.RandomState(0).choice(ids.numel(), 128, replace=False)
     for i, (x, qw, bias, act, y) in enumerate(calls):
         wq = qw.codes.cpu().numpy()
         ws = qw.scale_f32.cpu().numpy()
-        xq, xs = ocpu.quantize_tensor(x)
+        if isinstance(x, tuple):
+            xq, xs = x
+            if i > 0 and calls[i - 1][3] == "gelu":   # fc2: codes from fc1's epilogue partials
+                xq_o, xs_o = ocpu.quantize_tensor(calls[i - 1][4].reshape(xq.shape))
+                assert xs == xs_o, f"call {i}"
+                np.testing.assert_array_equal(xq, xq_o, err_msg=f"call {i}")
+        else:
+            xq, xs = ocpu.quantize_tensor(x)
         acc = ocpu.gemm_i8(xq[rows], wq)
         b = bias.numpy() if bias is not None else None
         yo = ocpu.epilogue(acc, xs, ws, b, ACTS[act])
@@ -60,6 +76,27 @@ def test_layerwise_bit_exact(model_and_ids, monkeypatch):
             np.testing.assert_allclose(yg, yo, rtol=1e-5, atol=1e-6, err_msg=f"call {i}")
         else:
             assert yg.tobytes() == yo.tobytes(), f"call {i}"
+
+
+def test_layernorm_quantize_vs_oracle(cuda_device):
+    """QActivation.layernorm (LayerNorm kernel + absmax partials + one quantize
+    pass) against numpy LayerNorm + the oracle's quantize: the scale within
+    1e-6 relative, the codes equal except where the two fp32 LayerNorms land
+    on opposite sides of a rounding boundary (then one code apart, rarely)."""
+    import kansaiml_b200 as kz
+    from kansaiml_b200 import quantize as kq
+    rs = np.random.RandomState(8)
+    x = (rs.standard_normal((4096, 256)) * 3 + 1).astype(np.float32)
+    g = rs.uniform(0.5, 1.5, 256).astype(np.float32)
+    b = rs.standard_normal(256).astype(np.float32) * 0.1
+    qa = kq.QActivation.layernorm(kz.from_numpy(x), kz.from_numpy(g), kz.from_numpy(b), 1e-5)
+    ln = _ln(x) * g + b
+    q_o, s_o = ocpu.quantize_tensor(ln.astype(np.float32))
+    assert abs(qa.scale - s_o) <= 1e-6 * s_o
+    codes = qa.codes.cpu().numpy()
+    diff = np.abs(codes.astype(np.int32) - q_o.reshape(codes.shape).astype(np.int32))
+    assert diff.max() <= 1
+    assert (diff != 0).mean() <= 1e-3
 
 
 def _ln(x, eps=1e-5):
