@@ -6,15 +6,16 @@ Workload ("config 2"): one per-channel int8
 quantized Linear, fp32 weight [4096, 4096] ~ N(0, 0.02) quantized once per
 output channel, fp32 activations [2048, 4096] ~ N(0, 1).  One step = one
 forward of that layer over one batch of 2048 tokens: per-tensor activation
-absmax + quantize (2 HBM-bound kernels), then the tcgen05 int8 GEMM with the
-per-row x per-channel rescale fused into its epilogue, fp32 output.  Weight
+absmax + quantize (one HBM-bound cooperative launch), then the tcgen05 int8
+GEMM with the per-row x per-channel rescale fused into its epilogue, fp32
+output.  Weight
 quantization is the layer's one-time construction (QLinear.__init__), as in
 the reference (quantize.py:139-141), and is not in the step.
 
 Inputs exceed L2: 4 rotating sets of (X fp32, weight codes, Y fp32) = 336 MB,
-so every step reads cold data.  Timing: W warm-up steps, then K steps between
-barrier + synchronize on both sides, CUDA events on the launching stream, max
-over ranks.  N > 1 (torchrun): activations row-sharded, weights replicated:
+so every step reads cold data.  Timing: W warm-up steps, then K steps (CUDA
+graphs of 8 steps replayed back to back) between barrier + synchronize on
+both sides, CUDA events on the launching stream, max over ranks.  N > 1 (torchrun): activations row-sharded, weights replicated:
 every rank runs its own 2048-token batch, no collective on the data path
 ("weak" scaling).
 
