@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
+                    help="stack workload, N > 1: all-gather overlapped with the GEMM (peer, default) or plain NCCL")
     ap.add_argument("--workload", choices=["linear", "stack", "transformer", "sweep", "mlp"], default="linear",
                     help="linear: config 2 (default); stack: config 5, column-sharded 4-layer stack; "
                          "transformer: config 3 decoder; sweep: config 4 square GEMMs; mlp: config 1")
@@ -485,7 +487,7 @@ def run_stack(args, rank, world, local_rank, dev):
         g.manual_seed(5000 + l)
         return torch.randn((STACK_D, STACK_D), generator=g, device=dev) * 0.01
 
-    stack = ShardedQLinearStack([weight] * STACK_L, mesh)
+    stack = ShardedQLinearStack([weight] * STACK_L, mesh, exchange=args.exchange)
     g = torch.Generator(device=dev)
     g.manual_seed(77)
     x = torch.randn((STACK_M, STACK_D), generator=g, device=dev)
@@ -509,6 +511,7 @@ def run_stack(args, rank, world, local_rank, dev):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        stack.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -524,6 +527,7 @@ def run_stack(args, rank, world, local_rank, dev):
         "config": {"workload": "config5: 4 x int8 Linear [16384 -> 16384] column-sharded, 8192 tokens, per-tensor "
                                "activation quant + NCCL all-gather between layers",
                    "global_batch": STACK_M, "seq_len": None, "parallelism": f"tp{world} (column-sharded weights)",
+                   "exchange": stack.exchange,
                    "l2": "inputs larger than L2 (weights 1 GiB int8 in total, activations 512 MiB fp32)"},
         "tops": tops,
         "roofline": {"kernel": "whole stack", "bound": "tensor", "achieved": tops, "peak": 2.0 * bf16 * world,

@@ -195,6 +195,46 @@ int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K
                const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
                uint32_t* absmax_partials, kz_stream_t stream);
 
+/* kz_gemm_i8 with its A operand in the blocked layout [G][M][a_kblock]
+ * (G = K / a_kblock <= 32) still being assembled while the kernel runs (no
+ * reference counterpart; config 5's all-gather overlapped with the next
+ * layer's GEMM).  Block first_block is resident at launch.  The other blocks
+ * arrive in row chunks of flag_rows rows (a multiple of 128, or >= M for whole
+ * blocks): before a tile's first load from rows chunk c of block g the TMA
+ * producer waits until a_ready[g * C + c] (device memory, uint32,
+ * C = ceil(M / flag_rows)) equals ready_token -- a bounded wait: after 1 s the
+ * kernel records KZ_ERR_DEVICE_TIMEOUT and unwinds.  Every tile walks the K
+ * blocks starting at first_block, so the GEMM computes on resident data while
+ * the rest arrives (kz_copy_and_flag).  a_kblock must be a multiple of 128. */
+int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
+                     const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
+                     const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
+                     uint32_t* absmax_partials, const uint32_t* a_ready, uint32_t ready_token, int first_block,
+                     int64_t flag_rows, kz_stream_t stream);
+
+/* ------------------------------------------------- peer exchange buffers
+ * No reference counterpart (the reference's DTensor moves shards through host
+ * lists, python/kansai/distributed.py:157-176).  One process per GPU: a rank
+ * allocates device memory it will share (kz_peer_alloc: cudaMalloc plus a
+ * KZ_IPC_HANDLE_BYTES CUDA IPC handle), sends the handle to the other ranks
+ * of the node, which map it (kz_peer_open: peer access over NVLink).  No
+ * multicast object is created.  kz_peer_close unmaps a peer's buffer,
+ * kz_peer_free releases one's own (after every peer closed it). */
+#define KZ_IPC_HANDLE_BYTES 64
+int kz_peer_alloc(size_t bytes, void** ptr, void* handle_out);
+int kz_peer_open(const void* handle, void** ptr);
+int kz_peer_close(void* ptr);
+int kz_peer_free(void* ptr);
+
+/* On `stream`: copy `bytes` from src (this GPU's memory or a peer's mapped by
+ * kz_peer_open) to dst, then write `token` (< 65536) into *flag (a uint32 in
+ * this GPU's memory), ordered after the copy's data.  Neither step uses an SM
+ * (the copy runs on a copy engine, the flag is a stream memory write, or a
+ * 4-byte copy from a pinned host table where the driver lacks that), so they
+ * make progress while a kernel holding every SM waits on the flag -- the
+ * producer side of kz_gemm_i8_gated.  bytes == 0 publishes the flag only. */
+int kz_copy_and_flag(void* dst, const void* src, size_t bytes, uint32_t* flag, uint32_t token, kz_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

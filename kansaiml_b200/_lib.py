@@ -22,6 +22,7 @@ KZ_ERR_DEVICE_TIMEOUT = 5
 
 KZ_ACT_NONE, KZ_ACT_RELU, KZ_ACT_GELU = 0, 1, 2
 KZ_PARTIALS_WORDS = 1024
+KZ_IPC_HANDLE_BYTES = 64
 
 _P, _I64, _I, _D, _F, _U64, _SZ = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_double,
                                     ctypes.c_float, ctypes.c_uint64, ctypes.c_size_t)
@@ -45,6 +46,13 @@ SIGNATURES = {
     "kz_dequantize_cols_i8_f32": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "kz_qlinear_w8a32_f32": (_I, [_P, _I64, _I64, _P, _D, _P, _I64, _I, _P, _P]),
     "kz_gemm_i8": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P]),
+    "kz_gemm_i8_gated": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P,
+                              ctypes.c_uint32, _I, _I64, _P]),
+    "kz_peer_alloc": (_I, [_SZ, ctypes.POINTER(_P), _P]),
+    "kz_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "kz_peer_close": (_I, [_P]),
+    "kz_peer_free": (_I, [_P]),
+    "kz_copy_and_flag": (_I, [_P, _P, _SZ, _P, ctypes.c_uint32, _P]),
 }
 
 _lib = None

@@ -138,6 +138,44 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
     return true;
 }
 
+// ---- flags published by other agents
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait (whole warp; lane 0 polls) until *flag == token, for a flag another
+// agent publishes after the data it guards (here a copy engine, after a
+// peer-to-peer block copy).  Bounded like mbar_wait: on expiry records
+// KZ_ERR_DEVICE_TIMEOUT, raises abort_flag and returns false.  On success the
+// acquire is followed by a proxy fence, so the warp's later TMA (async proxy)
+// loads see the guarded data.
+__device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t token, int* status, volatile int* abort_flag) {
+    uint32_t ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t n = 0;
+        while (ld_acquire_sys_u32(flag) != token) {
+            __nanosleep(200);
+            if ((++n & 31u) == 0) {
+                if (abort_flag && *abort_flag) {
+                    ok = 0;
+                    break;
+                }
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    record_status(status, KZ_ERR_DEVICE_TIMEOUT);
+                    if (abort_flag) *abort_flag = 1;
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (ok) asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // ---- TMA (no multicast anywhere in this library)
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -77,6 +77,15 @@ struct GemmParams {
     int tma_out;        // 1: the single output goes through the TMA-store tensor map
     uint32_t* partials;
     int* status;
+    // Gated A (kz_gemm_i8_gated): rows [c * flag_rows, (c + 1) * flag_rows) of
+    // block g of the [G][M][a_kblock] A layout may be loaded once
+    // a_ready[g * flag_chunks + c] == ready_token; block first_block is
+    // resident from the start and every tile walks the blocks from it.
+    // NULL: no gating.
+    const uint32_t* a_ready;
+    uint32_t ready_token;
+    int first_block;
+    int flag_rows, flag_chunks;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
@@ -211,16 +220,30 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             tile_coords(t, p, tm, tn);
             const int m0 = tm * C::BM_TILE + (int)rank * C::BM_CTA;   // this CTA's A rows
             const int nb0 = tn * BN + (int)rank * C::BN_CTA;          // this CTA's B rows
-            const int rot = k_rotation(t, p);
+            const int rot = p.a_ready ? p.first_block * (p.a_kblock / BK) : k_rotation(t, p);
+            const int chunk = p.a_ready ? min(m0, p.M - 1) / p.flag_rows : 0;   // this CTA's rows lie in one chunk
+            int cur_g = -1;
             for (int kb = 0; kb < p.num_kb; ++kb) {
+                int kr = kb + rot;
+                if (kr >= p.num_kb) kr -= p.num_kb;
+                if (p.a_ready) {
+                    // first load of this tile from an A block: wait until its rows have landed
+                    const int g = (kr * BK) / p.a_kblock;
+                    if (g != cur_g) {
+                        cur_g = g;
+                        if (g != p.first_block &&
+                            !flag_wait(p.a_ready + g * p.flag_chunks + chunk, p.ready_token, p.status, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
                 if (!warp_wait<false>(empty0 + 8 * stage, phase ^ 1, p.status, abort_flag)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) {
                     if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, (PAIR ? 2 : 1) * C::STAGE_BYTES);
-                    int kr = kb + rot;
-                    if (kr >= p.num_kb) kr -= p.num_kb;
                     const int kbyte = kr * BK;
                     int ax = kbyte, ay = m0;
                     if (p.a_kblock != p.K) {
@@ -664,10 +687,11 @@ static int max_active_pairs(int dev) {
 
 using namespace kz;
 
-extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
-                          const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
-                          const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
-                          uint32_t* absmax_partials, kz_stream_t stream) {
+static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
+                        const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
+                        const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
+                        uint32_t* absmax_partials, const uint32_t* a_ready, uint32_t ready_token, int first_block,
+                        int64_t flag_rows, kz_stream_t stream) {
     KZ_REQUIRE(M >= 0 && N >= 0 && K >= 0, "kz_gemm_i8: negative dimension");
     KZ_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "kz_gemm_i8: dimension too large");
     KZ_REQUIRE(K <= 131072, "kz_gemm_i8: K > 131072 could overflow the int32 accumulator");
@@ -707,6 +731,11 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     p.ldo = ldo;
     p.partials = absmax_partials;
     p.status = device_status_ptr();
+    p.a_ready = a_ready;
+    p.ready_token = ready_token;
+    p.first_block = first_block;
+    p.flag_rows = (int)std::min<int64_t>(std::max<int64_t>(flag_rows, 1), std::max<int64_t>(M, 1));
+    p.flag_chunks = (int)((M + p.flag_rows - 1) / p.flag_rows);
 
     if (K == 0) {
         int grid = (int)std::min<int64_t>((M * N + 255) / 256, (int64_t)sm_count() * 4);
@@ -718,6 +747,13 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     KZ_REQUIRE(K % 16 == 0, "kz_gemm_i8: K must be a multiple of 16 (TMA row pitch)");
     KZ_REQUIRE(K % p.a_kblock == 0, "kz_gemm_i8: a_kblock must divide K");
     KZ_REQUIRE(p.a_kblock == K || p.a_kblock % 128 == 0, "kz_gemm_i8: a_kblock must be K or a multiple of 128");
+    if (a_ready) {
+        KZ_REQUIRE(p.a_kblock % 128 == 0 && K / p.a_kblock <= 32,
+                   "kz_gemm_i8_gated: a_kblock must be a multiple of 128 with at most 32 blocks");
+        KZ_REQUIRE(first_block >= 0 && first_block < K / p.a_kblock, "kz_gemm_i8_gated: first_block out of range");
+        KZ_REQUIRE(flag_rows >= M || (flag_rows > 0 && flag_rows % 128 == 0),
+                   "kz_gemm_i8_gated: flag_rows must be >= M or a positive multiple of 128");
+    }
     KZ_REQUIRE((reinterpret_cast<uintptr_t>(A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0,
                "kz_gemm_i8: A and B must be 16-byte aligned");
     // CTA pairs (256-row tiles) unless the whole problem fits one 128-row tile
@@ -779,4 +815,22 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
     if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, false>(grid, s, ent, p);
     if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, false>(grid, s, ent, p);
     return launch_gemm<KZ_ACT_NONE, false>(grid, s, ent, p);
+}
+
+extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
+                          const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
+                          const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
+                          uint32_t* absmax_partials, kz_stream_t stream) {
+    return gemm_i8_impl(A, B, M, N, K, a_kblock, row_scale, rs_stride, col_scale, cs_stride, bias, act, out_f32,
+                        out_i32, ldo, absmax_partials, nullptr, 0, 0, 0, stream);
+}
+
+extern "C" int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
+                                const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
+                                const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
+                                uint32_t* absmax_partials, const uint32_t* a_ready, uint32_t ready_token,
+                                int first_block, int64_t flag_rows, kz_stream_t stream) {
+    KZ_REQUIRE(a_ready != nullptr, "kz_gemm_i8_gated: a_ready is NULL");
+    return gemm_i8_impl(A, B, M, N, K, a_kblock, row_scale, rs_stride, col_scale, cs_stride, bias, act, out_f32,
+                        out_i32, ldo, absmax_partials, a_ready, ready_token, first_block, flag_rows, stream);
 }

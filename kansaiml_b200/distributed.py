@@ -29,7 +29,17 @@ quantize the local output columns -> all-gather of the int8 codes into the
 rank-major layout [G][M][N/G], which the next GEMM reads directly (a_kblock =
 N/G).  Sharding changes no arithmetic: the result equals the unsharded stack
 bit for bit.
+
+With NCCL on GPUs the all-gather is overlapped with the next GEMM
+(``exchange="peer"``, the default there): every rank quantizes its columns
+straight into block g of a buffer the other ranks have mapped (CUDA IPC over
+NVLink); after a one-word barrier the copy engines pull the other ranks' blocks
+into the local buffer, publishing a token per block, while the next GEMM
+starts on the local block and waits (bounded) on each token before its first
+load from that block.  ``exchange="collective"`` keeps the plain NCCL
+all-gather.
 """
+import ctypes
 import threading
 
 import torch
@@ -38,6 +48,7 @@ import torch.distributed as dist
 from . import _lib
 from .quantize import (QTensor, gemm_i8_device, new_partials, quantize_cols_device, quantize_partials_device,
                        quantize_tensor_device)
+from .tensor import ptr, stream_handle
 from .tensor import Tensor, as_tensor, cat
 
 
@@ -286,6 +297,87 @@ def column_shard_bounds(total, rank, world):
 
 # -------------------------------------------------- config 5: sharded stack
 
+class _PeerGather:
+    """Two [G][M][Kb] int8 gather buffers per rank (one per layer parity),
+    exported to the other ranks through CUDA IPC.  Rank g writes block g of its
+    own buffer; ``pull`` copies the other ranks' blocks into the local one on a
+    side stream (copy engines), in row chunks of ``rows`` rows -- chunk 0 of
+    every block first, then chunk 1, ... (the order the GEMM's first tiles need
+    them) -- publishing ``token`` in flags[parity, h * chunks + c] after each."""
+
+    def __init__(self, M, kb, world, rank, group, device):
+        self.lib = _lib.load()
+        self.world, self.rank, self.group, self.device = world, rank, group, device
+        self.block = M * kb
+        self.kb = kb
+        per = -(-M // 8)                          # about 8 chunks, each a multiple of 128 rows
+        self.rows = -(-per // 128) * 128 if M > 128 else M
+        self.chunks = -(-M // self.rows)
+        own, handles = [], []
+        for _ in range(2):
+            p, h = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.KZ_IPC_HANDLE_BYTES)
+            _lib.check(self.lib.kz_peer_alloc(world * self.block, ctypes.byref(p), h), "kz_peer_alloc")
+            own.append(p.value)
+            handles.append(h.raw)
+        self.own = own
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handles, group=group)
+        self.peer = []
+        for r in range(world):
+            if r == rank:
+                self.peer.append(list(own))
+                continue
+            ptrs = []
+            for i in range(2):
+                p = ctypes.c_void_p()
+                _lib.check(self.lib.kz_peer_open(gathered[r][i], ctypes.byref(p)), "kz_peer_open")
+                ptrs.append(p.value)
+            self.peer.append(ptrs)
+        self.flags = torch.zeros((2, world * self.chunks), dtype=torch.int32, device=device)
+        self.side = torch.cuda.Stream(device)
+        self.one = torch.zeros(1, dtype=torch.int32, device=device)
+        self.token = 0
+
+    def own_block(self, parity):
+        return self.own[parity] + self.rank * self.block
+
+    def pull(self, parity):
+        """After every rank wrote its block: barrier, then copy the other
+        ranks' blocks in ring order.  Returns (A pointer, flags, token)."""
+        stream = torch.cuda.current_stream(self.device)
+        dist.all_reduce(self.one, group=self.group)     # every rank's block is written
+        self.token = self.token % 65535 + 1
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        side = self.side
+        side.wait_event(ready)
+        flags = self.flags[parity]
+        M = self.block // self.kb
+        for c in range(self.chunks):
+            r0 = c * self.rows
+            nbytes = (min(M, r0 + self.rows) - r0) * self.kb
+            for j in range(1, self.world):
+                h = (self.rank + j) % self.world
+                off = h * self.block + r0 * self.kb
+                _lib.check(self.lib.kz_copy_and_flag(self.own[parity] + off, self.peer[h][parity] + off, nbytes,
+                                                     flags.data_ptr() + 4 * (h * self.chunks + c), self.token,
+                                                     side.cuda_stream), "kz_copy_and_flag")
+        return self.own[parity], flags, self.token
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for r in range(self.world):
+            if r != self.rank:
+                for p in self.peer[r]:
+                    _lib.check(self.lib.kz_peer_close(ctypes.c_void_p(p)), "kz_peer_close")
+        dist.barrier(group=self.group)
+        for p in self.own:
+            _lib.check(self.lib.kz_peer_free(ctypes.c_void_p(p)), "kz_peer_free")
+        self.own, self.peer = [], []
+
+
 class ShardedQLinearStack:
     """A stack of bias-free int8 Linear layers, weights column-sharded over the
     ranks of an SPMD mesh (or a single GPU when the mesh is None).
@@ -295,7 +387,7 @@ class ShardedQLinearStack:
     keeps only its columns, quantized per output channel.  N / G must be a
     multiple of 128 between layers (the GEMM's K block)."""
 
-    def __init__(self, weights, mesh=None):
+    def __init__(self, weights, mesh=None, exchange=None):
         self.mesh = mesh
         self.world = len(mesh) if mesh is not None and mesh.is_spmd else 1
         self.rank = mesh.rank if mesh is not None and mesh.is_spmd else 0
@@ -322,6 +414,19 @@ class ShardedQLinearStack:
             if n_loc % 128:
                 raise ValueError("out_features / mesh size must be a multiple of 128")
         self.partials = None
+        if exchange is None:
+            exchange = "peer" if (self.group is not None or self.world > 1) and dist.get_backend(self.group) == "nccl" \
+                else "collective"
+        if exchange not in ("peer", "collective"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange = exchange if self.world > 1 else "collective"
+        self._peer = None
+
+    def close(self):
+        """Release the peer exchange buffers (collective over the mesh)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def forward(self, x, return_local=True):
         """x: fp32 [M, K] replicated on every rank.  Returns the last layer's
@@ -334,16 +439,34 @@ class ShardedQLinearStack:
         M = xd.shape[0]
         a, _, a_s32 = quantize_tensor_device(xd)
         a_kblock = xd.shape[1]
+        gate = None
         y = None
         for li, (qt, K, N) in enumerate(self.layers):
             n_loc = qt.shape[1]
             last = li == len(self.layers) - 1
-            y, _ = gemm_i8_device(a, qt.kmajor(), row_scale=a_s32, col_scale=qt.scale_f32, a_kblock=a_kblock, m=M,
-                                  partials=None if last else self.partials)
+            parts = None if last else self.partials
+            if gate is None:
+                y, _ = gemm_i8_device(a, qt.kmajor(), row_scale=a_s32, col_scale=qt.scale_f32, a_kblock=a_kblock, m=M,
+                                      partials=parts)
+            else:
+                y = self._gemm_gated(gate, M, K, a_kblock, qt, a_s32, parts)
+            gate = None
             if last:
                 break
             if self.world > 1:
                 allreduce_partials_max(self.partials, self.group)
+            if self.exchange == "peer":
+                if self._peer is None or self._peer.block != M * n_loc:
+                    self.close()
+                    self._peer = _PeerGather(M, n_loc, self.world, self.rank, self.group, dev)
+                parity = li % 2
+                s64 = torch.empty(1, dtype=torch.float64, device=dev)
+                a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
+                _lib.call("kz_quantize_partials_f32", ptr(y), y.numel(), ptr(self.partials),
+                          self._peer.own_block(parity), ptr(s64), ptr(a_s32), stream_handle(dev))
+                gate = self._peer.pull(parity)
+                a_kblock = n_loc
+                continue
             yq, _, a_s32 = quantize_partials_device(y, self.partials)
             if self.world > 1:
                 a = allgather_blocked(yq, self.group)   # [G, M, n_loc]
@@ -355,5 +478,15 @@ class ShardedQLinearStack:
             return Tensor(y)
         parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
         return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+
+    def _gemm_gated(self, gate, M, K, a_kblock, qt, a_s32, partials):
+        a_ptr, flags, token = gate
+        N = qt.shape[1]
+        dev = a_s32.device
+        out = torch.empty((M, N), dtype=torch.float32, device=dev)
+        _lib.call("kz_gemm_i8_gated", a_ptr, ptr(qt.kmajor()), M, N, K, a_kblock, ptr(a_s32), 0, ptr(qt.scale_f32), 1,
+                  None, _lib.KZ_ACT_NONE, ptr(out), None, N, ptr(partials), ptr(flags), token, self.rank,
+                  self._peer.rows, stream_handle(dev))
+        return out
 
     __call__ = forward

@@ -61,7 +61,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _spmd_worker(rank, world, port, q):
+def _spmd_worker(rank, world, port, q, exchange):
     try:
         import datetime
         import torch.distributed as dist
@@ -71,9 +71,15 @@ def _spmd_worker(rank, world, port, q):
                                 timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
         from kansaiml_b200.distributed import DeviceMesh, ShardedQLinearStack
         mesh = DeviceMesh.spmd()
-        stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh)
-        y = stack(torch.from_numpy(make_x()).cuda(), return_local=False).numpy()
-        q.put((rank, y))
+        stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh, exchange=exchange)
+        assert stack.exchange == exchange
+        x = torch.from_numpy(make_x()).cuda()
+        y = stack(x, return_local=False).numpy()
+        y2 = stack(x, return_local=False).numpy()   # buffers, flags and tokens reused
+        q.put((rank, y if y.tobytes() == y2.tobytes() else "second forward differs"))
+        from kansaiml_b200.quantize import device_status
+        assert device_status() == 0
+        stack.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001
@@ -81,11 +87,14 @@ def _spmd_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_stack_two_gpus_spmd_bit_exact(expected):
+@pytest.mark.parametrize("exchange", ["collective", "peer"])
+def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
+    """Two ranks over NCCL: the plain all-gather, and the all-gather overlapped
+    with the next GEMM (peer buffers + copy engines + the gated GEMM)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_spmd_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_spmd_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
