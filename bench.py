@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
-                    help="stack workload, N > 1: all-gather overlapped with the GEMM (peer, default) or plain NCCL")
+                    help="stack workload, N > 1: plain NCCL all-gather (collective, default) or the copy-engine "
+                         "all-gather overlapped with the gated GEMM (peer)")
     ap.add_argument("--workload", choices=["linear", "stack", "transformer", "sweep", "mlp"], default="linear",
                     help="linear: config 2 (default); stack: config 5, column-sharded 4-layer stack; "
                          "transformer: config 3 decoder; sweep: config 4 square GEMMs; mlp: config 1")
@@ -372,29 +373,30 @@ def main():
     # ------------------------------------------------------------ e2e
     # Through the public API with host buffers: every step copies its pinned
     # host X to the device, runs QLinear, and copies its fp32 Y back to pinned
-    # host memory.  Copies run on their own streams, double-buffered, so step
-    # i's upload, step i-1's forward and step i-2's download overlap (PCIe
-    # carries both directions at once); every step still moves its own bytes.
-    x_host = [torch.from_numpy(rs.standard_normal((M_TOK, K_IN)).astype(np.float32)).pin_memory() for _ in range(2)]
-    y_host = [torch.empty((M_TOK, N_OUT), dtype=torch.float32).pin_memory() for _ in range(2)]
-    x_dev = [torch.empty((M_TOK, K_IN), dtype=torch.float32, device=dev) for _ in range(2)]
-    y_dev = [None, None]
+    # host memory.  Copies run on their own streams over NB buffers, so step
+    # i's upload, earlier steps' forwards and downloads overlap (PCIe carries
+    # both directions at once); every step still moves its own bytes.
+    NB = 3
+    x_host = [torch.from_numpy(rs.standard_normal((M_TOK, K_IN)).astype(np.float32)).pin_memory() for _ in range(NB)]
+    y_host = [torch.empty((M_TOK, N_OUT), dtype=torch.float32).pin_memory() for _ in range(NB)]
+    x_dev = [torch.empty((M_TOK, K_IN), dtype=torch.float32, device=dev) for _ in range(NB)]
+    y_dev = [None] * NB
     layer = layers[0]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_fwd = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(NB)]
+    ev_fwd = [torch.cuda.Event() for _ in range(NB)]
+    ev_out = [torch.cuda.Event() for _ in range(NB)]
     for e in ev_fwd + ev_out:
         e.record(stream)
 
     def e2e_step(i):
-        b = i % 2
+        b = i % NB
         with torch.cuda.stream(s_in):
-            s_in.wait_event(ev_fwd[b])            # the forward that read x_dev[b] two steps ago is done
+            s_in.wait_event(ev_fwd[b])            # the forward that read x_dev[b] NB steps ago is done
             x_dev[b].copy_(x_host[b], non_blocking=True)
             ev_in[b].record(s_in)
         stream.wait_event(ev_in[b])
-        stream.wait_event(ev_out[b])              # y_dev[b] of two steps ago has been read back
+        stream.wait_event(ev_out[b])              # y_dev[b] of NB steps ago has been read back
         y_dev[b] = layer(kz.Tensor(x_dev[b])).data
         ev_fwd[b].record(stream)
         with torch.cuda.stream(s_out):
