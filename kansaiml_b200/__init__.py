@@ -23,7 +23,7 @@ def build():
 
 
 def __getattr__(name):
-    if name in ("quantize", "nn", "distributed"):
+    if name in ("quantize", "nn", "distributed", "serialize", "workloads"):
         import importlib
         return importlib.import_module(f".{name}", __name__)
     raise AttributeError(name)

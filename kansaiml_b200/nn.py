@@ -29,9 +29,11 @@ class Module:
         raise NotImplementedError
 
     def named_parameters(self, prefix=""):
+        """nn.py:19-39: (dotted name, Tensor) for every trainable parameter
+        (requires_grad), recursing into sub-Modules and lists of them."""
         for name, value in vars(self).items():
             full = f"{prefix}{name}"
-            if isinstance(value, Tensor):
+            if isinstance(value, Tensor) and value.requires_grad:
                 yield full, value
             elif isinstance(value, Module):
                 yield from value.named_parameters(full + ".")
@@ -52,8 +54,8 @@ class Linear(Module):
 
     def __init__(self, in_features, out_features, seed=0, device=None):
         std = 1.0 / math.sqrt(in_features)
-        self.weight = randn([in_features, out_features], std=std, seed=seed, device=device)
-        self.bias = zeros([out_features], device=device)
+        self.weight = randn([in_features, out_features], std=std, requires_grad=True, seed=seed, device=device)
+        self.bias = zeros([out_features], requires_grad=True, device=device)
 
     def forward(self, x):
         return as_tensor(x).matmul(self.weight).add(self.bias)
@@ -96,8 +98,8 @@ class LayerNorm(Module):
     def __init__(self, num_features, eps=1e-5, device=None):
         self.num_features = num_features
         self.eps = eps
-        self.weight = ones([num_features], device=device)
-        self.bias = zeros([num_features], device=device)
+        self.weight = ones([num_features], requires_grad=True, device=device)
+        self.bias = zeros([num_features], requires_grad=True, device=device)
 
     def forward(self, x):
         t = as_tensor(x).data
@@ -113,7 +115,7 @@ class Embedding(Module):
     takes (nested) integer ids."""
 
     def __init__(self, num_embeddings, embedding_dim, seed=0, device=None):
-        self.weight = randn([num_embeddings, embedding_dim], std=1.0, seed=seed, device=device)
+        self.weight = randn([num_embeddings, embedding_dim], std=1.0, requires_grad=True, seed=seed, device=device)
 
     def forward(self, ids):
         idx = ids if isinstance(ids, torch.Tensor) else torch.as_tensor(ids, dtype=torch.long)
@@ -136,10 +138,10 @@ class MultiHeadAttention(Module):
             raise ValueError(f"MultiHeadAttention: d_model={d_model} must be divisible by num_heads={num_heads}")
         self.d_model, self.num_heads, self.d_k = d_model, num_heads, d_model // num_heads
         std = 1.0 / math.sqrt(d_model)
-        self.w_q = randn([d_model, d_model], std=std, seed=seed, device=device)
-        self.w_k = randn([d_model, d_model], std=std, seed=seed + 1, device=device)
-        self.w_v = randn([d_model, d_model], std=std, seed=seed + 2, device=device)
-        self.w_o = randn([d_model, d_model], std=std, seed=seed + 3, device=device)
+        self.w_q = randn([d_model, d_model], std=std, requires_grad=True, seed=seed, device=device)
+        self.w_k = randn([d_model, d_model], std=std, requires_grad=True, seed=seed + 1, device=device)
+        self.w_v = randn([d_model, d_model], std=std, requires_grad=True, seed=seed + 2, device=device)
+        self.w_o = randn([d_model, d_model], std=std, requires_grad=True, seed=seed + 3, device=device)
         self.q_proj = None
         self.qkv = None
 

@@ -18,6 +18,12 @@ from .quantize import QActivation, QLinear
 from .tensor import Tensor, from_numpy
 
 
+def _param(a, device):
+    t = from_numpy(a, device)
+    t.requires_grad = True
+    return t
+
+
 class Decoder(nn.Module):
     """Config 3 decoder.  ``fp32`` keeps the unquantized weights (numpy) so a
     CPU restatement can rebuild the same model."""
@@ -37,10 +43,10 @@ class Decoder(nn.Module):
             blk = nn.TransformerBlock(d_model, heads, d_ff, seed=seed + 10 + i, device=device)
             w = {name: normal(d_model, d_model) for name in ("w_q", "w_k", "w_v", "w_o")}
             for name, value in w.items():
-                setattr(blk.attn, name, from_numpy(value, device))
+                setattr(blk.attn, name, _param(value, device))
             w["fc1"], w["fc2"] = normal(d_model, d_ff), normal(d_ff, d_model)
-            blk.fc1.weight = from_numpy(w["fc1"], device)
-            blk.fc2.weight = from_numpy(w["fc2"], device)
+            blk.fc1.weight = _param(w["fc1"], device)
+            blk.fc2.weight = _param(w["fc2"], device)
             w["fc1_b"], w["fc2_b"] = blk.fc1.bias.numpy(), blk.fc2.bias.numpy()
             blk.quantize(per_channel=True, activations="int8")
             self.blocks.append(blk)
@@ -48,7 +54,7 @@ class Decoder(nn.Module):
         self.ln = nn.LayerNorm(d_model, device=device)
         head = nn.Linear(d_model, vocab, seed=seed + 99, device=device)
         self.fp32["head"], self.fp32["head_b"] = normal(d_model, vocab), head.bias.numpy()
-        head.weight = from_numpy(self.fp32["head"], device)
+        head.weight = _param(self.fp32["head"], device)
         self.head = QLinear(head, per_channel=True, activations="int8")
         self.mask = nn.causal_mask(ctx, device=device)
 
