@@ -266,6 +266,68 @@ def dtensor_run(fn, output_placement, *dtensor_args):
     return DTensor(mesh, output_placement, results)
 
 
+def _all_reduce_sum(tensors):
+    """distributed.py:268-287: element-wise sum of same-shape tensors.  The
+    reference adds the fp32 values as Python floats (double) in device order
+    and narrows the total to fp32 once; the same here, on the first tensor's
+    device."""
+    first = as_tensor(tensors[0])
+    dev = first.data.device
+    total = first.data.to(torch.float64)
+    for t in tensors[1:]:
+        total = total + as_tensor(t).data.to(dev, torch.float64)
+    return Tensor(total.to(torch.float32))
+
+
+def _all_reduce_sum_spmd(local, group=None):
+    """_all_reduce_sum across the ranks of an SPMD mesh: every rank's fp32
+    values are all-gathered (NCCL over NVLink, or gloo) and summed in double
+    in rank order, so every rank holds the reference's exact result."""
+    x = as_tensor(local).data.contiguous()
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x, group=group)
+    return _all_reduce_sum([Tensor(p) for p in parts])
+
+
+def dtensor_grad(grad_fn, wrt_placements, *dtensor_args):
+    """distributed.py:290-391 with a callable in place of the KIR graph:
+    ``grad_fn(*shards)`` returns this device's local gradients (one per
+    entry of wrt_placements), run per mesh device like dtensor_run; each
+    entry is combined by its placement -- Replicate(): all-reduce sum
+    (_all_reduce_sum), Shard(dim): concatenation along dim (an all-gather).
+    Returns one Tensor per entry."""
+    if not callable(grad_fn):
+        raise TypeError("dtensor_grad takes a callable (kansaiml_b200 has no KIR graphs)")
+    if not dtensor_args:
+        raise ValueError("dtensor_grad needs at least one DTensor argument")
+    mesh = dtensor_args[0].mesh
+    for dt in dtensor_args:
+        if dt.mesh is not mesh:
+            raise ValueError("all DTensor arguments must share the same DeviceMesh")
+
+    def as_tuple(out):
+        return tuple(out) if isinstance(out, (tuple, list)) else (out,)
+
+    per_device = [as_tuple(o) for o in dtensor_run(grad_fn, Replicate(), *dtensor_args).shards]
+    for out in per_device:
+        if len(out) != len(wrt_placements):
+            raise ValueError("grad_fn must return one gradient per entry of wrt_placements")
+    results = []
+    for j, placement in enumerate(wrt_placements):
+        local_j = [out[j] for out in per_device]
+        if isinstance(placement, Replicate):
+            if mesh.is_spmd:
+                results.append(_all_reduce_sum_spmd(local_j[0], mesh.group))
+            else:
+                results.append(_all_reduce_sum(local_j))
+        elif isinstance(placement, Shard):
+            results.append(DTensor(mesh, placement, [as_tensor(t) for t in local_j]).to_tensor())
+        else:
+            raise TypeError(f"unknown placement {placement!r}")
+    return results
+
+
 # --------------------------------------------------------- collectives
 
 def allreduce_partials_max(partials, group=None):

@@ -123,3 +123,86 @@ def test_gloo_collectives_world2():
         assert tuple(shape) == (2, 3, 2) and firsts == [1.0, 2.0]
         assert local_shape == [6, 2]
         assert back == np.arange(24, dtype=np.float32).tolist()
+
+
+def _sum_cases():
+    rs = np.random.RandomState(17)
+    # values whose fp32 sum depends on the order and precision of the adds
+    return [(rs.standard_normal(257) * 10.0 ** rs.uniform(-3, 3, 257)).astype(np.float32) for _ in range(3)]
+
+
+def test_all_reduce_sum_matches_reference():
+    """_all_reduce_sum (distributed.py:268-287): double adds in device order,
+    one narrowing to fp32; pinned against the reference's own function where
+    its checkout is available, else against the formula."""
+    from oracle import refpkg
+    parts = _sum_cases()
+    ours = kd._all_reduce_sum([kz.from_numpy(p, device="cpu") for p in parts]).numpy()
+    expect = np.asarray([float(a) + float(b) + float(c) for a, b, c in zip(*parts)], np.float64).astype(np.float32)
+    assert ours.tobytes() == expect.tobytes()
+    if refpkg.reference_available():
+        ref = refpkg.import_reference_kansai()
+        import sys
+        import kansai.distributed as rdist
+        core = sys.modules["kansai._core"]
+        r = rdist._all_reduce_sum([core.from_flat(p.tolist(), [p.size], False) for p in parts])
+        assert np.asarray(r.tolist(), np.float32).tobytes() == ours.tobytes()
+        assert ref is not None
+
+
+def test_dtensor_grad_threaded_cpu_mesh():
+    """Replicate() gradients all-reduce by sum, Shard(0) gradients concatenate."""
+    mesh = kd.DeviceMesh(["cpu", "cpu", "cpu"])
+    x = kz.from_flat(np.arange(7 * 4, dtype=np.float32) / 7, [7, 4], device="cpu")
+    dt = kd.DTensor.from_tensor(x, mesh, kd.Shard(0))
+
+    def grad_fn(shard):
+        t = shard.data
+        return kz.Tensor(t.sum(0)), kz.Tensor(t * 2)
+
+    gw, gx = kd.dtensor_grad(grad_fn, [kd.Replicate(), kd.Shard(0)], dt)
+    pieces = [p.data.sum(0).numpy() for p in kd._split_tensor(x, 0, 3)]
+    expect = (pieces[0].astype(np.float64) + pieces[1] + pieces[2]).astype(np.float32)
+    assert gw.numpy().tobytes() == expect.tobytes()
+    assert gx.numpy().tobytes() == (x.numpy() * 2).tobytes()
+    with pytest.raises(ValueError):
+        kd.dtensor_grad(lambda s: (s,), [kd.Replicate(), kd.Shard(0)], dt)
+
+
+def _gloo_grad_worker(rank, world, port, q):
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        mesh = kd.DeviceMesh.spmd()
+        parts = _sum_cases()
+        x = kz.from_flat(np.arange(6 * 4, dtype=np.float32), [6, 4], device="cpu")
+        dt = kd.DTensor.from_tensor(x, mesh, kd.Shard(0))
+
+        def grad_fn(shard):
+            return kz.from_numpy(parts[rank], device="cpu"), kz.Tensor(shard.data + 1)
+
+        gw, gx = kd.dtensor_grad(grad_fn, [kd.Replicate(), kd.Shard(0)], dt)
+        q.put((rank, gw.numpy().tobytes(), gx.numpy().tobytes()))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e), None))
+
+
+def test_dtensor_grad_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_grad_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, gw, gx = q.get(timeout=120)
+        res[r] = (gw, gx)
+    for p in procs:
+        p.join(timeout=60)
+    parts = _sum_cases()
+    expect = (parts[0].astype(np.float64) + parts[1]).astype(np.float32).tobytes()
+    for r in range(2):
+        assert res[r][1] is not None, res[r][0]
+        assert res[r][0] == expect
+        assert res[r][1] == (np.arange(24, dtype=np.float32) + 1).tobytes()
