@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
+    ap.add_argument("--exchange", choices=["peer", "collective", "fused"], default=None,
                     help="stack workload, N > 1: plain NCCL all-gather (collective, default) or the copy-engine "
                          "all-gather overlapped with the gated GEMM (peer)")
     ap.add_argument("--workload", choices=["linear", "stack", "transformer", "sweep", "mlp"], default="linear",

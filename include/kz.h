@@ -212,11 +212,32 @@ int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int
                      uint32_t* absmax_partials, const uint32_t* a_ready, uint32_t ready_token, int first_block,
                      int64_t flag_rows, kz_stream_t stream);
 
+/* Config 5's all-gather fused into the next layer's GEMM (no reference
+ * counterpart).  Rank `rank` of `world` (2..8) holds the full A operand's
+ * layout [world][M][K/world] in A (this GPU's memory), of which only block
+ * `rank` is filled at launch.  peer_A[h] / peer_flags[h] (h != rank) are rank
+ * h's own A buffer and flags array, mapped here with kz_peer_open (entry
+ * `rank` ignored).  The launch's first copy_ctas CTAs (even, 2..32) push this
+ * rank's block into every peer's A (TMA stores over NVLink) in row chunks of
+ * flag_rows rows (a multiple of 128 dividing M) and after each chunk write
+ * `token` into every peer's flags[rank * (M / flag_rows) + c]; the other CTAs
+ * run the GEMM of kz_gemm_i8_gated on the local flags (bounded waits, 1 s),
+ * starting every tile at block `rank`.  flags (this rank's, zeroed once)
+ * holds 2 * world * (M / flag_rows) words: the ready flags the peers write,
+ * then this rank's per-chunk arrival counters, left at zero.  Every rank's
+ * previous use of the A buffer must be finished before any rank launches (a
+ * barrier).  fp32 output with fused rescale, act none. */
+int kz_gemm_i8_allgather(const int8_t* A, int8_t* const* peer_A, uint32_t* const* peer_flags, int world, int rank,
+                         const int8_t* B, int64_t M, int64_t N, int64_t K, const float* row_scale, int64_t rs_stride,
+                         const float* col_scale, int64_t cs_stride, float* out_f32, int64_t ldo,
+                         uint32_t* absmax_partials, uint32_t* flags, uint32_t token, int64_t flag_rows, int copy_ctas,
+                         kz_stream_t stream);
+
 /* ------------------------------------------------- peer exchange buffers
  * No reference counterpart (the reference's DTensor moves shards through host
  * lists, python/kansai/distributed.py:157-176).  One process per GPU: a rank
- * allocates device memory it will share (kz_peer_alloc: cudaMalloc plus a
- * KZ_IPC_HANDLE_BYTES CUDA IPC handle), sends the handle to the other ranks
+ * allocates device memory it will share (kz_peer_alloc: zero-filled cudaMalloc
+ * plus a KZ_IPC_HANDLE_BYTES CUDA IPC handle), sends the handle to the other ranks
  * of the node, which map it (kz_peer_open: peer access over NVLink).  No
  * multicast object is created.  kz_peer_close unmaps a peer's buffer,
  * kz_peer_free releases one's own (after every peer closed it). */

@@ -48,6 +48,8 @@ SIGNATURES = {
     "kz_gemm_i8": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P]),
     "kz_gemm_i8_gated": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P,
                               ctypes.c_uint32, _I, _I64, _P]),
+    "kz_gemm_i8_allgather": (_I, [_P, _P, _P, _I, _I, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P,
+                                  ctypes.c_uint32, _I64, _I, _P]),
     "kz_peer_alloc": (_I, [_SZ, ctypes.POINTER(_P), _P]),
     "kz_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
     "kz_peer_close": (_I, [_P]),

@@ -28,6 +28,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "kz_common.cuh"
 
@@ -86,24 +87,37 @@ struct GemmParams {
     uint32_t ready_token;
     int first_block;
     int flag_rows, flag_chunks;
+    // Fused all-gather (kz_gemm_i8_allgather): CTAs [0, copy_ctas) copy the
+    // other ranks' A blocks from their memory into the local [G][M][a_kblock]
+    // buffer, chunk by chunk, and publish ready_token in copy_flags (== a_ready)
+    // for the computing CTAs.  0: no copy role.
+    int copy_ctas;
+    uint32_t* copy_flags;
+    int group_m;        // tile rasterisation: tile-rows per group
+};
+
+// The other ranks' gather buffers ([G][M][a_kblock] bytes in their memory,
+// mapped into this process) as TMA store targets, and their flag arrays;
+// entry `rank` unused.
+constexpr int kMaxPeers = 8;
+struct PeerMaps {
+    CUtensorMap dst[kMaxPeers];
+    uint32_t* flags[kMaxPeers];
+};
+struct NoPeerMaps {
+    int unused;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
-    const int group_size = gemm::GROUP_M * p.tiles_n;
+    const int group_size = p.group_m * p.tiles_n;
     const int group = t / group_size;
-    const int first_m = group * gemm::GROUP_M;
-    const int gm = min(gemm::GROUP_M, p.tiles_m - first_m);
+    const int first_m = group * p.group_m;
+    const int gm = min(p.group_m, p.tiles_m - first_m);
     const int r = t - group * group_size;
     tm = first_m + r % gm;
     tn = r / gm;
 }
 
-// First k-block of tile t.  Tiles that run at the same time start their k
-// loops at different k-blocks, so the SMs sharing an A row-band or a B
-// column-band do not all fetch the same L2 lines in the same moment.  The
-// int32 accumulation is exact, so the order of the k-blocks does not change
-// the result.
-__device__ __forceinline__ int k_rotation(int t, const GemmParams& p) { return (int)(((unsigned)t * 7u) % (unsigned)p.num_kb); }
 
 template <int ACT>
 __device__ __forceinline__ float epi_act_t(float v) {
@@ -133,10 +147,112 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* st
     return __all_sync(0xffffffffu, got);
 }
 
-template <int ACT, bool PAIR>
+__device__ __forceinline__ void st_release_gpu_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Copy role of the fused all-gather GEMM (push): one thread per copy CTA
+// streams 128-row x 128-byte tiles of this rank's own A block, local memory ->
+// shared memory (TMA load) -> every other rank's gather buffer (TMA stores into
+// peer memory over NVLink: posted writes, no round trip), 12 stages with about
+// 8 loads and 4 tiles' stores in flight.  Row chunks go in order, so the rows
+// the first GEMM tiles need land first; every chunk's tiles are dealt
+// round-robin over all copy CTAs.  A CTA reports its share of a chunk once its
+// stores have completed (checked D tiles later); the last copy CTA to report a
+// chunk resets the chunk's counter and writes ready_token into every other
+// rank's flags[rank * C + c].  Every wait is bounded; on expiry the thread
+// waits (bounded) for its copies in flight and returns.
+__device__ __forceinline__ void gemm_copy_role(const CUtensorMap& tmA, const PeerMaps& pm, const GemmParams& p,
+                                               uint8_t* smem) {
+    constexpr int S = 12, D = 4, DR = 4;
+    constexpr uint32_t TILE = 128 * 128;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * TILE);
+    const int G = p.K / p.a_kblock, C = p.flag_chunks, R = p.flag_rows, me = p.first_block;
+    const int xs_n = p.a_kblock / 128;
+    const int T = (R / 128) * xs_n;                 // tiles per chunk (>= copy_ctas, checked on the host)
+    const int64_t total = (int64_t)C * T;
+    const int cidx = blockIdx.x, cc = p.copy_ctas;
+    const int n = cidx < total ? (int)((total - cidx + cc - 1) / cc) : 0;
+    uint32_t* counters = p.copy_flags + G * C;     // this rank's per-chunk arrival counters
+    const uint32_t full0 = smem_u32(bars), stage0 = smem_u32(smem);
+    for (int s = 0; s < S; ++s) mbar_init(full0 + 8 * s, 1);
+    fence_mbarrier_init();
+
+    auto coords = [&](int i, int& c, int& x, int& row) {
+        const int64_t q = cidx + (int64_t)i * cc;
+        c = (int)(q / T);
+        const int w = (int)(q - (int64_t)c * T);
+        x = (w % xs_n) * 128;
+        row = c * R + (w / xs_n) * 128;
+    };
+    auto ends_chunk = [&](int i) {
+        const int64_t q = cidx + (int64_t)i * cc;
+        return i == n - 1 || (q / T) != ((q + cc) / T);
+    };
+    auto publish = [&](int i) {
+        int c, x, row;
+        coords(i, c, x, row);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence_system();
+        const uint32_t old = atomicAdd(counters + c, 1u);
+        if (old == (uint32_t)cc - 1) {
+            atomicExch(counters + c, 0u);
+            __threadfence_system();
+            for (int h = 0; h < G; ++h)
+                if (h != me) st_release_sys_u32(pm.flags[h] + me * C + c, p.ready_token);
+        }
+    };
+    auto issue = [&](int i) {
+        int c, x, row;
+        coords(i, c, x, row);
+        const uint32_t bar = full0 + 8 * (i % S);
+        mbar_arrive_expect_tx(bar, TILE);
+        tma_load_2d(stage0 + (uint32_t)(i % S) * TILE, &tmA, bar, x, me * p.M + row);
+    };
+    const int pro = min(S, n);
+    for (int i = 0; i < pro; ++i) issue(i);
+    int issued = pro;
+    bool ok = true;
+    int i = 0;
+    for (; i < n; ++i) {
+        if (!mbar_wait(full0 + 8 * (i % S), (uint32_t)((i / S) & 1), p.status, nullptr)) {
+            ok = false;
+            break;
+        }
+        int c, x, row;
+        coords(i, c, x, row);
+        for (int h = 0; h < G; ++h)
+            if (h != me) tma_store_2d(&pm.dst[h], stage0 + (uint32_t)(i % S) * TILE, x, me * p.M + row);
+        bulk_commit_group();               // one group per tile (all its peer stores)
+        if (i >= D && ends_chunk(i - D)) {
+            bulk_wait_group<D>();          // tiles up to i - D are stored everywhere
+            publish(i - D);
+        }
+        if (i >= DR && issued < n) {
+            bulk_wait_group_read<DR>();    // tiles up to i - DR have left their stages
+            issue(issued++);               // tile i - DR + S, into tile i - DR's stage
+        }
+    }
+    if (!ok) {
+        // unwinding: every load in flight lands before the CTA's shared memory goes away
+        for (int j = i + 1; j < issued; ++j) mbar_wait(full0 + 8 * (j % S), (uint32_t)((j / S) & 1), nullptr, nullptr);
+        bulk_wait_group_all();
+        return;
+    }
+    bulk_wait_group_all();
+    for (int j = max(0, n - D); j < n; ++j)
+        if (ends_chunk(j)) publish(j);
+}
+
+template <int ACT, bool PAIR, bool COPY = false>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmOut, const GemmParams p,
+                   const __grid_constant__ typename std::conditional<COPY, PeerMaps, NoPeerMaps>::type pm) {
     using namespace gemm;
     using C = Cfg<PAIR>;
     // The kernel has no static shared memory, so the dynamic region starts at
@@ -148,6 +264,19 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         return;
     }
     uint8_t* smem = smem_raw;
+    if constexpr (COPY) {
+        if ((int)blockIdx.x < p.copy_ctas) {
+            griddep_launch_dependents();
+            griddep_wait();
+            if (p.partials && threadIdx.x == 0) {
+                // copy CTAs own partials slots too (no output rows: zero)
+                p.partials[1 + blockIdx.x] = 0u;
+                if (blockIdx.x == 0) p.partials[0] = gridDim.x;
+            }
+            if (threadIdx.x == 0) gemm_copy_role(tmA, pm, p, smem);
+            return;
+        }
+    }
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_STAGE;
     uint8_t* sEpi = sB + C::STAGES * C::B_STAGE;
@@ -160,8 +289,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
     const bool leader = rank == 0;
-    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;     // scheduling unit: pair or CTA
-    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int cbase = COPY ? p.copy_ctas : 0;                               // copy CTAs come first
+    const int unit = PAIR ? (int)((blockIdx.x - cbase) >> 1) : (int)(blockIdx.x - cbase);   // pair or CTA
+    const int units = PAIR ? (int)((gridDim.x - cbase) >> 1) : (int)(gridDim.x - cbase);
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + C::STAGES);
     const uint32_t tfull0 = smem_u32(bars + 2 * C::STAGES), tempty0 = smem_u32(bars + 2 * C::STAGES + NUM_ACC);
     const uint32_t drain = smem_u32(bars + 2 * C::STAGES + 2 * NUM_ACC);
@@ -220,7 +350,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             tile_coords(t, p, tm, tn);
             const int m0 = tm * C::BM_TILE + (int)rank * C::BM_CTA;   // this CTA's A rows
             const int nb0 = tn * BN + (int)rank * C::BN_CTA;          // this CTA's B rows
-            const int rot = p.a_ready ? p.first_block * (p.a_kblock / BK) : k_rotation(t, p);
+            // Every tile walks K from the same k-block, so tiles running at the
+            // same time read the same k-slices of their A and B panels (they
+            // stay in L2); a gated A starts at the block already resident.  The
+            // int32 accumulation is exact, so the k order does not change the
+            // result.
+            const int rot = p.a_ready ? p.first_block * (p.a_kblock / BK) : 0;
             const int chunk = p.a_ready ? min(m0, p.M - 1) / p.flag_rows : 0;   // this CTA's rows lie in one chunk
             int cur_g = -1;
             for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -590,9 +725,9 @@ static int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint6
     return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, cols, rows, cols, box_cols, box_rows);
 }
 
-template <int ACT, bool PAIR>
+template <int ACT, bool PAIR, bool COPY = false>
 static int set_smem_attr() {
-    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<ACT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    KZ_CHECK_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<ACT, PAIR, COPY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        gemm::Cfg<PAIR>::SMEM_BYTES));
     return KZ_OK;
 }
@@ -606,6 +741,7 @@ static int ensure_gemm_attrs(int dev) {
     if (!st) st = set_smem_attr<KZ_ACT_NONE, true>();
     if (!st) st = set_smem_attr<KZ_ACT_RELU, true>();
     if (!st) st = set_smem_attr<KZ_ACT_GELU, true>();
+    if (!st) st = set_smem_attr<KZ_ACT_NONE, true, true>();
     if (st) return st;
     if (dev >= 0 && dev < 64) done[dev] = 1;
     return KZ_OK;
@@ -636,8 +772,9 @@ constexpr int kTmapCache = 16;
 thread_local TmapEntry t_tmap_cache[kTmapCache];
 thread_local int t_tmap_next = 0;
 
-template <int ACT, bool PAIR>
-static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const GemmParams& p) {
+template <int ACT, bool PAIR, bool COPY = false>
+static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const GemmParams& p,
+                       const PeerMaps* peers = nullptr) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(gemm::THREADS);
@@ -655,7 +792,12 @@ static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const Gem
         attr[1].val.clusterDim.z = 1;
         cfg.numAttrs = 2;
     }
-    KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<ACT, PAIR>, ent->a, ent->b, ent->out, p));
+    if constexpr (COPY) {
+        KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<ACT, PAIR, true>, ent->a, ent->b, ent->out, p, *peers));
+    } else {
+        KZ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<ACT, PAIR, false>, ent->a, ent->b, ent->out, p,
+                                         NoPeerMaps{0}));
+    }
     return KZ_OK;
 }
 
@@ -691,7 +833,8 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
                         const float* row_scale, int64_t rs_stride, const float* col_scale, int64_t cs_stride,
                         const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
                         uint32_t* absmax_partials, const uint32_t* a_ready, uint32_t ready_token, int first_block,
-                        int64_t flag_rows, kz_stream_t stream) {
+                        int64_t flag_rows, int8_t* const* peers, uint32_t* const* peer_flags, int copy_ctas,
+                        kz_stream_t stream) {
     KZ_REQUIRE(M >= 0 && N >= 0 && K >= 0, "kz_gemm_i8: negative dimension");
     KZ_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "kz_gemm_i8: dimension too large");
     KZ_REQUIRE(K <= 131072, "kz_gemm_i8: K > 131072 could overflow the int32 accumulator");
@@ -736,6 +879,11 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
     p.first_block = first_block;
     p.flag_rows = (int)std::min<int64_t>(std::max<int64_t>(flag_rows, 1), std::max<int64_t>(M, 1));
     p.flag_chunks = (int)((M + p.flag_rows - 1) / p.flag_rows);
+    p.copy_ctas = peers ? copy_ctas : 0;
+    p.copy_flags = const_cast<uint32_t*>(a_ready);
+    // Gated A arrives in row chunks: group as many tile-rows as one chunk
+    // holds, so the first tiles need the first chunk only.
+    p.group_m = a_ready ? std::max(1, std::min(gemm::GROUP_M, p.flag_rows / 256)) : gemm::GROUP_M;
 
     if (K == 0) {
         int grid = (int)std::min<int64_t>((M * N + 255) / 256, (int64_t)sm_count() * 4);
@@ -801,12 +949,28 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
 
     int grid;
     if (pair) {
-        const int pairs = std::min(p.num_tiles, max_active_pairs(dev));
+        const int pairs = std::min(p.num_tiles, max_active_pairs(dev) - p.copy_ctas / 2);
         grid = 2 * pairs;
     } else {
         grid = std::min(p.num_tiles, sm_count());
     }
-    if (grid > KZ_PARTIALS_WORDS - 3) grid = (KZ_PARTIALS_WORDS - 3) & ~1;
+    if (grid > KZ_PARTIALS_WORDS - 3 - p.copy_ctas) grid = (KZ_PARTIALS_WORDS - 3 - p.copy_ctas) & ~1;
+    if (peers) {
+        // fused all-gather: peer tensor maps, copy CTAs in front of the computing pairs
+        KZ_REQUIRE(pair && act == KZ_ACT_NONE, "kz_gemm_i8_allgather: needs M > 128 and act none");
+        PeerMaps pm;
+        memset(&pm, 0, sizeof(pm));
+        const int G = (int)(K / p.a_kblock);
+        for (int h = 0; h < G; ++h) {
+            if (h == first_block) continue;
+            KZ_REQUIRE(peers[h] && (reinterpret_cast<uintptr_t>(peers[h]) & 15u) == 0 && peer_flags[h],
+                       "kz_gemm_i8_allgather: peer buffers must be non-NULL and 16-byte aligned, peer flags non-NULL");
+            st = make_tmap_i8(&pm.dst[h], peers[h], (uint64_t)p.a_kblock, (uint64_t)M * G, 128, 128);
+            if (st) return st;
+            pm.flags[h] = peer_flags[h];
+        }
+        return launch_gemm<KZ_ACT_NONE, true, true>(grid + p.copy_ctas, s, ent, p, &pm);
+    }
     if (pair) {
         if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, true>(grid, s, ent, p);
         if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, true>(grid, s, ent, p);
@@ -822,7 +986,7 @@ extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N
                           const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
                           uint32_t* absmax_partials, kz_stream_t stream) {
     return gemm_i8_impl(A, B, M, N, K, a_kblock, row_scale, rs_stride, col_scale, cs_stride, bias, act, out_f32,
-                        out_i32, ldo, absmax_partials, nullptr, 0, 0, 0, stream);
+                        out_i32, ldo, absmax_partials, nullptr, 0, 0, 0, nullptr, nullptr, 0, stream);
 }
 
 extern "C" int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,
@@ -832,5 +996,27 @@ extern "C" int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int
                                 int first_block, int64_t flag_rows, kz_stream_t stream) {
     KZ_REQUIRE(a_ready != nullptr, "kz_gemm_i8_gated: a_ready is NULL");
     return gemm_i8_impl(A, B, M, N, K, a_kblock, row_scale, rs_stride, col_scale, cs_stride, bias, act, out_f32,
-                        out_i32, ldo, absmax_partials, a_ready, ready_token, first_block, flag_rows, stream);
+                        out_i32, ldo, absmax_partials, a_ready, ready_token, first_block, flag_rows, nullptr, nullptr,
+                        0, stream);
+}
+
+extern "C" int kz_gemm_i8_allgather(const int8_t* A, int8_t* const* peer_A, uint32_t* const* peer_flags, int world,
+                                    int rank, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* row_scale,
+                                    int64_t rs_stride, const float* col_scale, int64_t cs_stride, float* out_f32,
+                                    int64_t ldo, uint32_t* absmax_partials, uint32_t* flags, uint32_t token,
+                                    int64_t flag_rows, int copy_ctas, kz_stream_t stream) {
+    KZ_REQUIRE(peer_A && peer_flags && flags, "kz_gemm_i8_allgather: peer_A, peer_flags and flags must be non-NULL");
+    KZ_REQUIRE(world >= 2 && world <= kMaxPeers && K % world == 0, "kz_gemm_i8_allgather: need 2 <= world <= 8 and world | K");
+    KZ_REQUIRE(rank >= 0 && rank < world, "kz_gemm_i8_allgather: rank out of range");
+    KZ_REQUIRE(copy_ctas >= 2 && copy_ctas % 2 == 0 && copy_ctas <= 32, "kz_gemm_i8_allgather: copy_ctas must be even, 2..32");
+    KZ_REQUIRE(flag_rows > 0 && flag_rows % 128 == 0 && M % flag_rows == 0,
+               "kz_gemm_i8_allgather: flag_rows must be a multiple of 128 dividing M");
+    KZ_REQUIRE((K / world) % 128 == 0, "kz_gemm_i8_allgather: K / world must be a multiple of 128");
+    // every unit (row chunk of one rank's block) has at least one tile per copy CTA
+    const int64_t tiles_per_unit = (flag_rows / 128) * ((K / world) / 128);
+    if (copy_ctas > tiles_per_unit) copy_ctas = (int)std::max<int64_t>(2, tiles_per_unit & ~1ll);
+    KZ_REQUIRE(copy_ctas <= tiles_per_unit, "kz_gemm_i8_allgather: row chunks too small for two copy CTAs");
+    return gemm_i8_impl(A, B, M, N, K, K / world, row_scale, rs_stride, col_scale, cs_stride, nullptr, KZ_ACT_NONE,
+                        out_f32, nullptr, ldo, absmax_partials, flags, token, rank, flag_rows, peer_A, peer_flags,
+                        copy_ctas, stream);
 }

@@ -68,6 +68,11 @@ extern "C" int kz_peer_alloc(size_t bytes, void** ptr, void* handle_out) {
     if (st) return st;
     void* p = nullptr;
     KZ_CHECK_CUDA(cudaMalloc(&p, bytes));
+    cudaError_t zerr = cudaMemset(p, 0, bytes);
+    if (zerr != cudaSuccess) {
+        cudaFree(p);
+        return cuda_error(zerr, "cudaMemset");
+    }
     cudaIpcMemHandle_t h;
     cudaError_t err = cudaIpcGetMemHandle(&h, p);
     if (err != cudaSuccess) {

@@ -39,7 +39,15 @@ local block and waits (bounded) on each chunk's token before its first load
 from it.  Measured on B200s it wins at 2 GPUs (4.06 vs 4.12 ms per 4-layer
 forward) and loses at 4 and 8 (2.69 vs 2.57, 3.55 vs 2.52 ms): the copy
 engines move about 470 GB/s per GPU, below NCCL's SM-driven NVLink transfers.
-The default is therefore ``exchange="collective"``, the NCCL all-gather.
+``exchange="fused"`` moves the all-gather into the GEMM launch itself
+(kz_gemm_i8_allgather): its first CTAs push this rank's block into every other
+rank's buffer over NVLink (TMA stores into peer memory), chunk by chunk, and
+raise the peers' flags, while the other CTAs compute on the chunks already
+present.  Bit-exact, but on B200s at 2 GPUs a launch with 8 copy CTAs took
+about 1.0 ms per layer against 0.8 ms for the NCCL all-gather plus the plain
+GEMM: one copy CTA moves only about 20 GB/s, and the copy traffic slows the
+computing CTAs even when nothing waits.  The default is
+``exchange="collective"``, the NCCL all-gather.
 """
 import ctypes
 import threading
@@ -374,36 +382,57 @@ class _PeerGather:
         self.world, self.rank, self.group, self.device = world, rank, group, device
         self.block = M * kb
         self.kb = kb
-        per = -(-M // 8)                          # about 8 chunks, each a multiple of 128 rows
-        self.rows = -(-per // 128) * 128 if M > 128 else M
+        # about 8 row chunks, each a multiple of 128 rows dividing M (M % 128 == 0)
+        m128 = M // 128
+        d = next(v for v in range(-(-m128 // 8), m128 + 1) if m128 % v == 0)
+        self.rows = d * 128
         self.chunks = -(-M // self.rows)
+        # two gather buffers (one per layer parity) and, for the fused GEMM, one
+        # flags buffer per parity (ready flags the peers write, then counters)
+        self.flag_words = 2 * world * self.chunks
+        sizes = [world * self.block, world * self.block, 4 * self.flag_words, 4 * self.flag_words]
         own, handles = [], []
-        for _ in range(2):
+        for nbytes in sizes:
             p, h = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.KZ_IPC_HANDLE_BYTES)
-            _lib.check(self.lib.kz_peer_alloc(world * self.block, ctypes.byref(p), h), "kz_peer_alloc")
+            _lib.check(self.lib.kz_peer_alloc(nbytes, ctypes.byref(p), h), "kz_peer_alloc")
             own.append(p.value)
             handles.append(h.raw)
-        self.own = own
+        self.own, self.xflags = own[:2], own[2:]
         gathered = [None] * world
         dist.all_gather_object(gathered, handles, group=group)
-        self.peer = []
+        self.peer, self.peer_xflags = [], []
         for r in range(world):
             if r == rank:
-                self.peer.append(list(own))
+                self.peer.append(list(self.own))
+                self.peer_xflags.append(list(self.xflags))
                 continue
             ptrs = []
-            for i in range(2):
+            for i in range(len(sizes)):
                 p = ctypes.c_void_p()
                 _lib.check(self.lib.kz_peer_open(gathered[r][i], ctypes.byref(p)), "kz_peer_open")
                 ptrs.append(p.value)
-            self.peer.append(ptrs)
-        self.flags = torch.zeros((2, world * self.chunks), dtype=torch.int32, device=device)
+            self.peer.append(ptrs[:2])
+            self.peer_xflags.append(ptrs[2:])
+        # per parity: world * chunks ready flags, then as many arrival counters
+        self.flags = torch.zeros((2, 2 * world * self.chunks), dtype=torch.int32, device=device)
         self.side = torch.cuda.Stream(device)
         self.one = torch.zeros(1, dtype=torch.int32, device=device)
         self.token = 0
 
     def own_block(self, parity):
         return self.own[parity] + self.rank * self.block
+
+    def fused(self, parity):
+        """After every rank finished with the buffers of this parity: barrier,
+        then the arguments of kz_gemm_i8_allgather (local buffer, the peers'
+        buffers and flags, local flags, token)."""
+        dist.all_reduce(self.one, group=self.group)
+        self.token = self.token % 65535 + 1
+        peer_a = (ctypes.c_void_p * self.world)(*[
+            self.peer[h][parity] if h != self.rank else 0 for h in range(self.world)])
+        peer_f = (ctypes.c_void_p * self.world)(*[
+            self.peer_xflags[h][parity] if h != self.rank else 0 for h in range(self.world)])
+        return self.own[parity], peer_a, peer_f, self.xflags[parity], self.token
 
     def pull(self, parity):
         """After every rank wrote its block: barrier, then copy the other
@@ -434,12 +463,12 @@ class _PeerGather:
         dist.barrier(group=self.group)
         for r in range(self.world):
             if r != self.rank:
-                for p in self.peer[r]:
+                for p in self.peer[r] + self.peer_xflags[r]:
                     _lib.check(self.lib.kz_peer_close(ctypes.c_void_p(p)), "kz_peer_close")
         dist.barrier(group=self.group)
-        for p in self.own:
+        for p in self.own + self.xflags:
             _lib.check(self.lib.kz_peer_free(ctypes.c_void_p(p)), "kz_peer_free")
-        self.own, self.peer = [], []
+        self.own, self.xflags, self.peer, self.peer_xflags = [], [], [], []
 
 
 class ShardedQLinearStack:
@@ -480,11 +509,12 @@ class ShardedQLinearStack:
         self.partials = None
         if exchange is None:
             exchange = "collective"
-        if exchange not in ("peer", "collective"):
+        if exchange not in ("peer", "collective", "fused"):
             raise ValueError(f"unknown exchange {exchange!r}")
-        if exchange == "peer" and self.world > 1 and dist.get_backend(self.group) != "nccl":
-            raise ValueError('exchange="peer" needs an NCCL mesh on GPUs')
+        if exchange != "collective" and self.world > 1 and dist.get_backend(self.group) != "nccl":
+            raise ValueError(f'exchange="{exchange}" needs an NCCL mesh on GPUs')
         self.exchange = exchange if self.world > 1 else "collective"
+        self.copy_ctas = 8
         self._peer = None
 
     def close(self):
@@ -513,6 +543,8 @@ class ShardedQLinearStack:
             if gate is None:
                 y, _ = gemm_i8_device(a, qt.kmajor(), row_scale=a_s32, col_scale=qt.scale_f32, a_kblock=a_kblock, m=M,
                                       partials=parts)
+            elif self.exchange == "fused":
+                y = self._gemm_fused(gate, M, K, qt, a_s32, parts)
             else:
                 y = self._gemm_gated(gate, M, K, a_kblock, qt, a_s32, parts)
             gate = None
@@ -520,7 +552,7 @@ class ShardedQLinearStack:
                 break
             if self.world > 1:
                 allreduce_partials_max(self.partials, self.group)
-            if self.exchange == "peer":
+            if self.exchange in ("peer", "fused") and M % 128 == 0:
                 if self._peer is None or self._peer.block != M * n_loc:
                     self.close()
                     self._peer = _PeerGather(M, n_loc, self.world, self.rank, self.group, dev)
@@ -529,7 +561,7 @@ class ShardedQLinearStack:
                 a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
                 _lib.call("kz_quantize_partials_f32", ptr(y), y.numel(), ptr(self.partials),
                           self._peer.own_block(parity), ptr(s64), ptr(a_s32), stream_handle(dev))
-                gate = self._peer.pull(parity)
+                gate = self._peer.pull(parity) if self.exchange == "peer" else self._peer.fused(parity)
                 a_kblock = n_loc
                 continue
             yq, _, a_s32 = quantize_partials_device(y, self.partials)
@@ -543,6 +575,16 @@ class ShardedQLinearStack:
             return Tensor(y)
         parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
         return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+
+    def _gemm_fused(self, gate, M, K, qt, a_s32, partials):
+        a_ptr, peer_a, peer_f, flags, token = gate
+        N = qt.shape[1]
+        dev = a_s32.device
+        out = torch.empty((M, N), dtype=torch.float32, device=dev)
+        _lib.call("kz_gemm_i8_allgather", a_ptr, peer_a, peer_f, self.world, self.rank, ptr(qt.kmajor()), M, N, K,
+                  ptr(a_s32), 0, ptr(qt.scale_f32), 1, ptr(out), N, ptr(partials), flags, token, self._peer.rows,
+                  self.copy_ctas, stream_handle(dev))
+        return out
 
     def _gemm_gated(self, gate, M, K, a_kblock, qt, a_s32, partials):
         a_ptr, flags, token = gate

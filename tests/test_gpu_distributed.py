@@ -87,10 +87,11 @@ def _spmd_worker(rank, world, port, q, exchange):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange", ["collective", "peer"])
+@pytest.mark.parametrize("exchange", ["collective", "peer", "fused"])
 def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
-    """Two ranks over NCCL: the plain all-gather, and the all-gather overlapped
-    with the next GEMM (peer buffers + copy engines + the gated GEMM)."""
+    """Two ranks over NCCL: the plain all-gather; the all-gather overlapped
+    with the next GEMM (peer buffers + copy engines + the gated GEMM); and the
+    all-gather inside the GEMM launch (copy CTAs pulling peer blocks by TMA)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
