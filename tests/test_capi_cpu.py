@@ -73,3 +73,39 @@ def test_workspace_size_query():
     lib = _lib.load()
     assert lib.kz_quantize_cols_workspace_bytes(4096, 4096) >= 4 * 4096
     assert lib.kz_quantize_cols_workspace_bytes(0, 5) == 0
+
+
+def test_exchange_entry_points_validate_arguments_without_gpu():
+    """The overlapped-exchange entry points reject bad arguments before any
+    device work, with a message."""
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    one = P(16)
+    # gated GEMM: ready flags are required
+    assert lib.kz_gemm_i8_gated(one, one, 256, 256, 512, 256, one, 0, one, 1, None, 0, one, None, 256, None, None,
+                                1, 0, 256, None) == 1
+    assert "a_ready" in _lib.last_error()
+    peers = (P * 2)(one, one)
+
+    def allgather(**kw):
+        args = dict(world=2, rank=0, M=512, N=256, K=512, flag_rows=128, copy_ctas=8)
+        args.update(kw)
+        return lib.kz_gemm_i8_allgather(one, peers, peers, args["world"], args["rank"], one, args["M"], args["N"],
+                                        args["K"], one, 0, one, 1, one, args["N"], None, one, 1, args["flag_rows"],
+                                        args["copy_ctas"], None)
+    assert allgather(world=1) == 1 and "world" in _lib.last_error()
+    assert allgather(world=9) == 1
+    assert allgather(rank=2) == 1 and "rank" in _lib.last_error()
+    assert allgather(copy_ctas=7) == 1 and "copy_ctas" in _lib.last_error()
+    assert allgather(flag_rows=100) == 1 and "flag_rows" in _lib.last_error()
+    assert allgather(flag_rows=384) == 1                     # does not divide M
+    assert allgather(K=384) == 1                             # K / world not a multiple of 128
+    # copy-engine transfer: flag required, token range
+    assert lib.kz_copy_and_flag(one, one, 16, None, 1, None) == 1 and "flag" in _lib.last_error()
+    assert lib.kz_copy_and_flag(one, one, 16, one, 70000, None) == 1 and "token" in _lib.last_error()
+    assert lib.kz_copy_and_flag(None, one, 16, one, 1, None) == 1
+    # peer buffers and LayerNorm
+    assert lib.kz_peer_alloc(16, None, None) == 1
+    assert lib.kz_peer_open(None, None) == 1
+    assert lib.kz_layernorm_partials_f32(one, 4, 0, None, None, ctypes.c_float(1e-5), one, one, None) == 1
+    assert lib.kz_layernorm_partials_f32(one, 4, 8, None, None, ctypes.c_float(1e-5), one, None, None) == 1
