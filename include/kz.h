@@ -218,7 +218,8 @@ int kz_gemm_i8_gated(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int
  * `rank` is filled at launch.  peer_A[h] / peer_flags[h] (h != rank) are rank
  * h's own A buffer and flags array, mapped here with kz_peer_open (entry
  * `rank` ignored).  The launch's first copy_ctas CTAs (even, 2..32) push this
- * rank's block into every peer's A (TMA stores over NVLink) in row chunks of
+ * rank's block into every peer's A (stores into peer memory over NVLink) in
+ * row chunks of
  * flag_rows rows (a multiple of 128 dividing M) and after each chunk write
  * `token` into every peer's flags[rank * (M / flag_rows) + c]; the other CTAs
  * run the GEMM of kz_gemm_i8_gated on the local flags (bounded waits, 1 s),

@@ -101,7 +101,7 @@ struct GemmParams {
 // entry `rank` unused.
 constexpr int kMaxPeers = 8;
 struct PeerMaps {
-    CUtensorMap dst[kMaxPeers];
+    int8_t* peer_a[kMaxPeers];
     uint32_t* flags[kMaxPeers];
 };
 struct NoPeerMaps {
@@ -155,20 +155,21 @@ __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Copy role of the fused all-gather GEMM (push): one thread per copy CTA
-// streams 128-row x 128-byte tiles of this rank's own A block, local memory ->
-// shared memory (TMA load) -> every other rank's gather buffer (TMA stores into
-// peer memory over NVLink: posted writes, no round trip), 12 stages with about
-// 8 loads and 4 tiles' stores in flight.  Row chunks go in order, so the rows
-// the first GEMM tiles need land first; every chunk's tiles are dealt
-// round-robin over all copy CTAs.  A CTA reports its share of a chunk once its
-// stores have completed (checked D tiles later); the last copy CTA to report a
-// chunk resets the chunk's counter and writes ready_token into every other
-// rank's flags[rank * C + c].  Every wait is bounded; on expiry the thread
-// waits (bounded) for its copies in flight and returns.
+// Copy role of the fused all-gather GEMM (push), run by every thread of a copy
+// CTA: thread 0 streams 128-row x 128-byte tiles of this rank's own A block
+// from local memory into shared memory (TMA loads, 12 stages in flight); all
+// threads then write each tile into every other rank's gather buffer with
+// 16-byte stores into peer memory over NVLink (posted writes, many in flight;
+// the tile is read back from the 128B-swizzled stage).  Row chunks go in
+// order, so the rows the first GEMM tiles need land first; every chunk's
+// tiles are dealt round-robin over all copy CTAs.  After a CTA's last tile of a
+// chunk, every thread fences its stores at system scope, and the last copy CTA
+// to report the chunk resets the chunk's counter and writes ready_token into
+// every other rank's flags[rank * C + c].  Waits are bounded; on expiry the
+// CTA stops issuing, waits (bounded) for its loads in flight and returns.
 __device__ __forceinline__ void gemm_copy_role(const CUtensorMap& tmA, const PeerMaps& pm, const GemmParams& p,
                                                uint8_t* smem) {
-    constexpr int S = 12, D = 4, DR = 4;
+    constexpr int S = 12;
     constexpr uint32_t TILE = 128 * 128;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * TILE);
     const int G = p.K / p.a_kblock, C = p.flag_chunks, R = p.flag_rows, me = p.first_block;
@@ -179,8 +180,12 @@ __device__ __forceinline__ void gemm_copy_role(const CUtensorMap& tmA, const Pee
     const int n = cidx < total ? (int)((total - cidx + cc - 1) / cc) : 0;
     uint32_t* counters = p.copy_flags + G * C;     // this rank's per-chunk arrival counters
     const uint32_t full0 = smem_u32(bars), stage0 = smem_u32(smem);
-    for (int s = 0; s < S; ++s) mbar_init(full0 + 8 * s, 1);
-    fence_mbarrier_init();
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(full0 + 8 * s, 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
 
     auto coords = [&](int i, int& c, int& x, int& row) {
         const int64_t q = cidx + (int64_t)i * cc;
@@ -193,59 +198,52 @@ __device__ __forceinline__ void gemm_copy_role(const CUtensorMap& tmA, const Pee
         const int64_t q = cidx + (int64_t)i * cc;
         return i == n - 1 || (q / T) != ((q + cc) / T);
     };
-    auto publish = [&](int i) {
-        int c, x, row;
-        coords(i, c, x, row);
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        __threadfence_system();
-        const uint32_t old = atomicAdd(counters + c, 1u);
-        if (old == (uint32_t)cc - 1) {
-            atomicExch(counters + c, 0u);
-            __threadfence_system();
-            for (int h = 0; h < G; ++h)
-                if (h != me) st_release_sys_u32(pm.flags[h] + me * C + c, p.ready_token);
-        }
-    };
-    auto issue = [&](int i) {
+    auto issue = [&](int i) {   // thread 0
         int c, x, row;
         coords(i, c, x, row);
         const uint32_t bar = full0 + 8 * (i % S);
         mbar_arrive_expect_tx(bar, TILE);
         tma_load_2d(stage0 + (uint32_t)(i % S) * TILE, &tmA, bar, x, me * p.M + row);
     };
-    const int pro = min(S, n);
-    for (int i = 0; i < pro; ++i) issue(i);
-    int issued = pro;
-    bool ok = true;
+    if (tid == 0)
+        for (int i = 0; i < min(S, n); ++i) issue(i);
+    int issued = min(S, n);
     int i = 0;
     for (; i < n; ++i) {
-        if (!mbar_wait(full0 + 8 * (i % S), (uint32_t)((i / S) & 1), p.status, nullptr)) {
-            ok = false;
-            break;
-        }
+        const bool got = mbar_wait(full0 + 8 * (i % S), (uint32_t)((i / S) & 1), p.status, nullptr);
+        if (__syncthreads_or(!got)) break;
         int c, x, row;
         coords(i, c, x, row);
-        for (int h = 0; h < G; ++h)
-            if (h != me) tma_store_2d(&pm.dst[h], stage0 + (uint32_t)(i % S) * TILE, x, me * p.M + row);
-        bulk_commit_group();               // one group per tile (all its peer stores)
-        if (i >= D && ends_chunk(i - D)) {
-            bulk_wait_group<D>();          // tiles up to i - D are stored everywhere
-            publish(i - D);
+        const uint4* st = reinterpret_cast<const uint4*>(smem + (size_t)(i % S) * TILE);
+        const int64_t grow0 = (int64_t)me * p.M + row;
+        for (int v = tid; v < (int)(TILE / 16); v += nthr) {
+            const int r = v >> 3, c16 = v & 7;
+            const uint4 val = st[r * 8 + (c16 ^ (r & 7))];
+            const int64_t off = (grow0 + r) * p.a_kblock + x + c16 * 16;
+            for (int h = 0; h < G; ++h)
+                if (h != me) *reinterpret_cast<uint4*>(pm.peer_a[h] + off) = val;
         }
-        if (i >= DR && issued < n) {
-            bulk_wait_group_read<DR>();    // tiles up to i - DR have left their stages
-            issue(issued++);               // tile i - DR + S, into tile i - DR's stage
+        const bool last = ends_chunk(i);
+        if (last) __threadfence_system();          // this thread's stores of the chunk are visible
+        __syncthreads();                           // the stage is free, every thread's stores are fenced
+        if (tid == 0) {
+            if (issued < n) issue(issued++);
+            if (last) {
+                const uint32_t old = atomicAdd(counters + c, 1u);
+                if (old == (uint32_t)cc - 1) {
+                    atomicExch(counters + c, 0u);
+                    __threadfence_system();
+                    for (int h = 0; h < G; ++h)
+                        if (h != me) st_release_sys_u32(pm.flags[h] + me * C + c, p.ready_token);
+                }
+            }
         }
     }
-    if (!ok) {
+    if (i < n && tid == 0) {
         // unwinding: every load in flight lands before the CTA's shared memory goes away
         for (int j = i + 1; j < issued; ++j) mbar_wait(full0 + 8 * (j % S), (uint32_t)((j / S) & 1), nullptr, nullptr);
-        bulk_wait_group_all();
-        return;
     }
-    bulk_wait_group_all();
-    for (int j = max(0, n - D); j < n; ++j)
-        if (ends_chunk(j)) publish(j);
+    __syncthreads();
 }
 
 template <int ACT, bool PAIR, bool COPY = false>
@@ -273,7 +271,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                 p.partials[1 + blockIdx.x] = 0u;
                 if (blockIdx.x == 0) p.partials[0] = gridDim.x;
             }
-            if (threadIdx.x == 0) gemm_copy_role(tmA, pm, p, smem);
+            gemm_copy_role(tmA, pm, p, smem);
             return;
         }
     }
@@ -965,8 +963,7 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
             if (h == first_block) continue;
             KZ_REQUIRE(peers[h] && (reinterpret_cast<uintptr_t>(peers[h]) & 15u) == 0 && peer_flags[h],
                        "kz_gemm_i8_allgather: peer buffers must be non-NULL and 16-byte aligned, peer flags non-NULL");
-            st = make_tmap_i8(&pm.dst[h], peers[h], (uint64_t)p.a_kblock, (uint64_t)M * G, 128, 128);
-            if (st) return st;
+            pm.peer_a[h] = peers[h];
             pm.flags[h] = peer_flags[h];
         }
         return launch_gemm<KZ_ACT_NONE, true, true>(grid + p.copy_ctas, s, ent, p, &pm);

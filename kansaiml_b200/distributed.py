@@ -41,12 +41,11 @@ forward) and loses at 4 and 8 (2.69 vs 2.57, 3.55 vs 2.52 ms): the copy
 engines move about 470 GB/s per GPU, below NCCL's SM-driven NVLink transfers.
 ``exchange="fused"`` moves the all-gather into the GEMM launch itself
 (kz_gemm_i8_allgather): its first CTAs push this rank's block into every other
-rank's buffer over NVLink (TMA stores into peer memory), chunk by chunk, and
-raise the peers' flags, while the other CTAs compute on the chunks already
-present.  Bit-exact, but on B200s at 2 GPUs a launch with 8 copy CTAs took
-about 1.0 ms per layer against 0.8 ms for the NCCL all-gather plus the plain
-GEMM: one copy CTA moves only about 20 GB/s, and the copy traffic slows the
-computing CTAs even when nothing waits.  The default is
+rank's buffer over NVLink (stores into peer memory), chunk by chunk, and raise
+the peers' flags, while the other CTAs compute on the chunks already present.
+Bit-exact, but on B200s at 2 GPUs it stays about 5% behind the NCCL
+all-gather plus the plain GEMM: the copy CTAs take SMs from the GEMM and their
+traffic slows the computing CTAs even when nothing waits.  The default is
 ``exchange="collective"``, the NCCL all-gather.
 """
 import ctypes
