@@ -421,11 +421,13 @@ __global__ void __launch_bounds__(1024, 1) quantize_fused_kernel(const float* __
 // Shared-memory-resident variant of the fused quantize: block b owns the
 // contiguous chunk [b * chunk, (b + 1) * chunk) of x; the first `cap` bytes of
 // it arrive by bulk copy into shared memory (one HBM read at full bandwidth)
-// and stay there for both passes; any remainder beyond `cap` is read from
-// global memory in both passes.  x and q must be 16-byte aligned and chunk a
-// multiple of 16 elements.
+// in 32 KB pieces, each with its own mbarrier so that its absmax is taken
+// while the later pieces are still in flight, and stay there for both passes;
+// any remainder beyond `cap` is read from global memory in both passes.  x and
+// q must be 16-byte aligned and chunk a multiple of 16 elements.
 constexpr int kResidentBlock = 1024;
 constexpr uint32_t kBulkPiece = 32768;
+constexpr int kMaxPieces = 8;   // 8 x 32 KB covers the largest resident chunk (< 227 KB)
 
 __global__ void __launch_bounds__(kResidentBlock, 1)
     quantize_resident_kernel(const float* __restrict__ x, int64_t n, int64_t chunk, uint32_t cap_floats,
@@ -433,26 +435,28 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
                              float* scale_f32_out, int* status) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     float* xs = reinterpret_cast<float*>(smem_raw);
-    __shared__ uint64_t bar;
+    __shared__ uint64_t bars[kMaxPieces];   // one per bulk piece, so each piece is reduced as it lands
     __shared__ uint32_t red[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t e0 = blockIdx.x * chunk;
     const int64_t e1 = min(n, e0 + chunk);
     const int64_t len = max((int64_t)0, e1 - e0);
-    const uint32_t res = (uint32_t)min((int64_t)cap_floats, len & ~(int64_t)3);   // resident floats (x4)
-    const uint32_t bar_addr = smem_u32(&bar);
-    if (threadIdx.x == 0) {
-        mbar_init(bar_addr, 1);
-        fence_mbarrier_init();
-    }
+    // resident floats (x4; at most kMaxPieces pieces, checked on the host)
+    const uint32_t res = (uint32_t)min((int64_t)cap_floats, len & ~(int64_t)3);
+    const uint32_t pieces = (res * 4u + kBulkPiece - 1) / kBulkPiece;
+    const uint32_t bar0 = smem_u32(bars);
+    if (threadIdx.x < pieces) mbar_init(bar0 + 8 * threadIdx.x, 1);
+    if (threadIdx.x == 0) fence_mbarrier_init();
     __syncthreads();
     griddep_launch_dependents();
     griddep_wait();
-    if (threadIdx.x == 0 && res > 0) {
-        mbar_arrive_expect_tx(bar_addr, res * 4u);
+    if (threadIdx.x == 0) {
         const char* src = reinterpret_cast<const char*>(x + e0);
-        for (uint32_t off = 0; off < res * 4u; off += kBulkPiece)
-            bulk_load(smem_u32(smem_raw) + off, src + off, min(kBulkPiece, res * 4u - off), bar_addr);
+        for (uint32_t k = 0; k < pieces; ++k) {
+            const uint32_t off = k * kBulkPiece, bytes = min(kBulkPiece, res * 4u - off);
+            mbar_arrive_expect_tx(bar0 + 8 * k, bytes);
+            bulk_load(smem_u32(smem_raw) + off, src + off, bytes, bar0 + 8 * k);
+        }
     }
     // phase 1: absmax of the non-resident remainder while the copy is in flight.
     // When res < len the remainder starts at e0 + cap, a multiple of 16 elements.
@@ -465,11 +469,15 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
         m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
     }
     for (int64_t j = r0 + 4 * rem4 + threadIdx.x; j < e1; j += blockDim.x) m = max(m, abs_bits(x[j]));
+    // then each resident piece as soon as it has landed
     bool ok = true;
-    if (res > 0) ok = mbar_wait(bar_addr, 0, status, nullptr);
-    if (ok) {
-        const float4* xs4 = reinterpret_cast<const float4*>(xs);
-        for (uint32_t i = threadIdx.x; i < res / 4; i += blockDim.x) {
+    const float4* xs4 = reinterpret_cast<const float4*>(xs);
+    constexpr uint32_t kPieceVec = kBulkPiece / 16;   // float4 per piece
+    for (uint32_t k = 0; ok && k < pieces; ++k) {
+        ok = mbar_wait(bar0 + 8 * k, 0, status, nullptr);
+        if (!ok) break;
+        const uint32_t end = min(res / 4, (k + 1) * kPieceVec);
+        for (uint32_t i = k * kPieceVec + threadIdx.x; i < end; i += blockDim.x) {
             const float4 a = xs4[i];
             m = max(m, max(max(abs_bits(a.x), abs_bits(a.y)), max(abs_bits(a.z), abs_bits(a.w))));
         }
@@ -517,7 +525,6 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
     }
     // resident part: consecutive threads read consecutive 16 B of shared memory
     // (no bank conflicts) and store 4 codes each (128 B per warp).
-    const float4* xs4 = reinterpret_cast<const float4*>(xs);
     uint32_t* qw = reinterpret_cast<uint32_t*>(q + e0);
     constexpr uint32_t B = kResidentBlock;
     uint32_t i = threadIdx.x;
@@ -851,6 +858,7 @@ int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, 
         int64_t chunk = (n + G - 1) / G;
         chunk = (chunk + 15) / 16 * 16;
         const uint32_t cap = (uint32_t)((dyn / 4) & ~15);
+        KZ_REQUIRE((uint64_t)cap * 4 <= (uint64_t)kMaxPieces * kBulkPiece, "quantize: resident chunk over the piece count");
         cudaLaunchConfig_t rcfg = {};
         rcfg.gridDim = dim3((unsigned)G);
         rcfg.blockDim = dim3(kResidentBlock);
