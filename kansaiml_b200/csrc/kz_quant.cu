@@ -312,8 +312,8 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* partials, int* status) {
     if (threadIdx.x == 0) {
         uint32_t* word = partials + kBarrierWord;
         const uint32_t add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
-        __threadfence();                                // this block's partial is visible
-        const uint32_t old = atomicAdd(word, add);
+        uint32_t old;   // release: this block's partial is visible before the arrival
+        asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(word), "r"(add) : "memory");
         ok = 1;
         const uint64_t t0 = globaltimer_ns();
         uint32_t it = 0;
@@ -324,7 +324,8 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* partials, int* status) {
                 break;
             }
         }
-        __threadfence();
+        // the acquire load that saw the flip orders this block's later reads
+        // (the other threads' through the __syncthreads below)
     }
     __syncthreads();
     return ok != 0;
