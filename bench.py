@@ -275,23 +275,25 @@ def main():
     Y = [y.data_ptr() for y in ys]
     XQ, S64, S32, PP = xq.data_ptr(), s64.data_ptr(), s32.data_ptr(), partials.data_ptr()
 
-    def step(i, ev=None):
+    def quantize_only(i):
+        """The activation absmax + quantize of set i % NSETS (one cooperative launch)."""
+        sh = torch.cuda.current_stream(dev).cuda_stream
+        if lib.kz_quantize_tensor_f32(X[i % NSETS], n_el, XQ, S64, S32, PP, sh):
+            raise RuntimeError(_lib.last_error())
+
+    def gemm_only(i):
+        """The int8 GEMM with fused rescale of set i % NSETS."""
+        j = i % NSETS
+        sh = torch.cuda.current_stream(dev).cuda_stream
+        if lib.kz_gemm_i8(XQ, B[j][0], M_TOK, N_OUT, K_IN, K_IN, S32, 0, B[j][1], 1, None, 0, Y[j], None, N_OUT,
+                          None, sh):
+            raise RuntimeError(_lib.last_error())
+
+    def step(i):
         """One forward of the layer on rotating set i % NSETS: activation absmax +
         quantize (one cooperative launch), int8 GEMM with fused rescale."""
-        j = i % NSETS
-        stream = torch.cuda.current_stream(dev)
-        sh = stream.cuda_stream
-        if ev is not None:
-            ev[0].record(stream)
-        st = lib.kz_quantize_tensor_f32(X[j], n_el, XQ, S64, S32, PP, sh)
-        if ev is not None:
-            ev[1].record(stream)
-        st |= lib.kz_gemm_i8(XQ, B[j][0], M_TOK, N_OUT, K_IN, K_IN, S32, 0, B[j][1], 1, None, 0, Y[j], None,
-                             N_OUT, None, sh)
-        if ev is not None:
-            ev[2].record(stream)
-        if st:
-            raise RuntimeError(_lib.last_error())
+        quantize_only(i)
+        gemm_only(i)
 
     # first step eagerly (sets up per-device state), then check the device status
     step(0)
@@ -301,24 +303,26 @@ def main():
 
     # Timed steps run from CUDA graphs of S consecutive steps (2 kernel nodes
     # each, no event nodes), replayed back to back, as a model captures its
-    # layers.  A second pass replays NG one-step graphs whose event nodes time
-    # each kernel on the device, for the per-kernel and roofline figures.
+    # layers.  A second pass times each kernel alone: graphs of S launches of
+    # just that kernel over the same rotating sets, replayed back to back with
+    # CUDA events only around the replays (event nodes between the two kernels
+    # of a step would break their programmatic dependent launch and add the
+    # gaps to both), for the per-kernel and roofline figures.
     S = 8
-    NG = 16
     cap_stream = torch.cuda.Stream(dev)
 
-    def capture(idx, evs=None):
+    def capture(idx, fn=step):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=cap_stream):
             for i in idx:
-                step(i, evs)
+                fn(i)
         return gr
 
     K = args.steps
     chunk_graph = capture(range(S))
     tail_graph = capture(range(K % S)) if K % S else None
-    graph_evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)] for _ in range(NG)]
-    step_graphs = [capture([g], graph_evs[g]) for g in range(NG)]
+    quant_graph = capture(range(S), quantize_only)
+    gemm_graph = capture(range(S), gemm_only)
     torch.cuda.synchronize()
 
     # warm-up: at least W steps, through the same graphs the timed region replays
@@ -326,8 +330,6 @@ def main():
         chunk_graph.replay()
     if tail_graph is not None:
         tail_graph.replay()
-    for g in step_graphs:
-        g.replay()
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
@@ -344,15 +346,22 @@ def main():
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
-    # per-kernel device times: K more steps through the event-timed graphs
-    quant_ms, gemm_ms = [], []
-    for i in range(K):
-        step_graphs[i % NG].replay()
-        if i % NG == NG - 1 or i == K - 1:
-            torch.cuda.synchronize()
-            for e in graph_evs[: i % NG + 1]:
-                quant_ms.append(e[0].elapsed_time(e[1]))
-                gemm_ms.append(e[1].elapsed_time(e[2]))
+    # per-kernel device times: as many launches of each kernel alone as the timed region made
+    reps = max(1, K // S)
+
+    def kernel_ms(gr):
+        for _ in range(2):
+            gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / (reps * S)
+    quant_avg = kernel_ms(quant_graph)
+    gemm_avg = kernel_ms(gemm_graph)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -360,8 +369,6 @@ def main():
     ms_per_step = ms / K
     tokens = M_TOK * world
     value = tokens / (ms_per_step / 1e3)
-    gemm_avg = statistics.mean(gemm_ms)
-    quant_avg = statistics.mean(quant_ms)
     ops = 2.0 * M_TOK * N_OUT * K_IN
     hbm_gbs, bf16, bf16_sus, peak_src = peaks()
     int8_peak = 2.0 * bf16   # B200 int8 dense rate is 2x its bf16 dense rate
@@ -449,8 +456,8 @@ def main():
                      "unit": "TOP/s", "frac": tops / int8_peak, "traffic": traffic,
                      "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
                      "avg_launch_us": gemm_avg * 1e3,
-                     "timing": f"CUDA events around each kernel inside one-step graphs, {len(gemm_ms)} steps "
-                               "replayed right after the timed region",
+                     "timing": f"CUDA events around {reps} back-to-back replays of a graph of {S} launches of "
+                               "this kernel alone over the same rotating sets, right after the timed region",
                      "algorithmic": f"2*M*N*K = {ops:.3e} op per launch"},
         "kernels": {"quantize_activations": {"avg_us": quant_avg * 1e3, "bound": "hbm",
                                              "achieved_gbs": quant_bytes / (quant_avg / 1e3) / 1e9,
