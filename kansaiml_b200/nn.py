@@ -184,12 +184,16 @@ class MultiHeadAttention(Module):
     def _self_attention(self, x, mask):
         """One int8 GEMM for q, k and v, fp32 scaled dot-product attention
         (softmax(q k^T / sqrt(d_k) + mask) v in one kernel), int8 output
-        projection."""
+        projection.  A causal_mask() is passed as is_causal: keys past each
+        query get weight 0, exactly what its -1e9 entries give (every row keeps
+        its own position, so their exponentials underflow to 0), without
+        reading the mask or the key tiles past the diagonal."""
         b, s, _ = x.shape
         h, dk = self.num_heads, self.d_k
         qkv = self.qkv(x).data.reshape(b, s, 3, h, dk).permute(2, 0, 3, 1, 4)
-        m = as_tensor(mask).data if mask is not None else None
-        att = torch.nn.functional.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=m)
+        causal = getattr(mask, "causal", False)
+        m = as_tensor(mask).data if mask is not None and not causal else None
+        att = torch.nn.functional.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=m, is_causal=causal)
         merged = Tensor(att.transpose(1, 2).reshape(b, s, self.d_model))
         return self.q_proj[3](merged)
 
@@ -239,8 +243,16 @@ class TransformerBlock(Module):
         return x.add(self.fc2(QActivation.from_partials(h, partials)))
 
 
+class CausalMask(Tensor):
+    """A mask tensor known to be causal_mask()'s (or a leading square slice of
+    one): the fused self-attention passes it on as is_causal instead of reading
+    it."""
+    __slots__ = ()
+    causal = True
+
+
 def causal_mask(seq, device=None):
     """Additive causal mask [1, 1, seq, seq] (0 allowed, -1e9 masked), the
     convention of examples/tinyshakespeare/train_shakespeare.py:96-97."""
     vals = torch.full((seq, seq), -1e9, dtype=torch.float32).triu(1)
-    return from_flat(vals.reshape(-1).tolist(), [1, 1, seq, seq], device=device)
+    return CausalMask(from_flat(vals.reshape(-1).tolist(), [1, 1, seq, seq], device=device).data)

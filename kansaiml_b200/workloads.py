@@ -62,7 +62,7 @@ class Decoder(nn.Module):
         """ids: int64 [B, S] (S <= ctx) on the model's device -> logits [B, S, vocab]."""
         s = ids.shape[1]
         x = Tensor(self.tok.weight.data[ids] + self.pos.weight.data[:s])
-        mask = self.mask if s == self.ctx else Tensor(self.mask.data[:, :, :s, :s])
+        mask = self.mask if s == self.ctx else nn.CausalMask(self.mask.data[:, :, :s, :s].contiguous())
         for blk in self.blocks:
             x = blk(x, mask=mask)
         ln = self.ln

@@ -99,6 +99,23 @@ def test_layernorm_quantize_vs_oracle(cuda_device):
     assert (diff != 0).mean() <= 1e-3
 
 
+def test_causal_flag_matches_the_explicit_mask(cuda_device):
+    """causal_mask() reaches attention as is_causal.  Its -1e9 entries give
+    weight exactly 0 (every row keeps its own position, so the shifted
+    exponentials underflow), so the result agrees with the explicit mask's to
+    fp32 rounding."""
+    from kansaiml_b200 import nn as knn
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    q, k, v = (torch.randn((4, 4, 256, 64), device="cuda", generator=g) for _ in range(3))
+    mask = knn.causal_mask(256, device="cuda")
+    assert getattr(mask, "causal", False)
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    flagged = sdpa(q, k, v, is_causal=True)
+    explicit = sdpa(q, k, v, attn_mask=mask.data)
+    torch.testing.assert_close(flagged, explicit, rtol=1e-5, atol=1e-6)
+
+
 def _ln(x, eps=1e-5):
     mean = x.mean(-1, keepdims=True, dtype=np.float32)
     c = x - mean

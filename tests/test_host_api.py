@@ -60,3 +60,17 @@ def test_qtensor_reference_constructor_and_nbytes():
     assert pc.codes.shape == (3, 2)          # stored K-major [N, K]
     assert pc.q == [1, 2, 3, 4, 5, 6]         # read back in the [K, N] layout
     assert pc.scale == [0.1, 0.2, 0.3]
+
+
+def test_causal_mask_values_and_marker():
+    """causal_mask(seq) holds the reference's additive causal mask (0 on and
+    below the diagonal, -1e9 above it; train_shakespeare.py:96-97) and carries
+    the causal marker the fused self-attention keys on; a plain Tensor of the
+    same values does not."""
+    from kansaiml_b200 import nn
+    m = nn.causal_mask(5, device="cpu")
+    assert getattr(m, "causal", False) and isinstance(m, kz.Tensor)
+    assert m.shape == [1, 1, 5, 5]
+    want = np.triu(np.full((5, 5), -1e9, np.float32), 1)
+    np.testing.assert_array_equal(np.asarray(m.tolist(), np.float32).reshape(5, 5), want)
+    assert not getattr(kz.Tensor(m.data.clone()), "causal", False)
