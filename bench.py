@@ -240,7 +240,19 @@ def main():
     dev = torch.device("cuda", local_rank)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        # The communicator's set-up prints a version banner on stdout (file
+        # descriptor 1); stdout carries only rank 0's JSON line, so fd 1
+        # points at stderr while the group and its communicator come up.
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
     if args.workload != "linear":
         {"stack": run_stack, "transformer": run_transformer, "sweep": run_sweep, "mlp": run_mlp}[args.workload](
             args, rank, world, local_rank, dev)
