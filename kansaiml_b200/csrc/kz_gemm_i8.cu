@@ -26,6 +26,7 @@
 // KZ_ERR_DEVICE_TIMEOUT and unwinds.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -730,8 +731,11 @@ static int set_smem_attr() {
     return KZ_OK;
 }
 
+// Per-device first-call state below is atomic: host threads of a threaded
+// mesh may make their first calls at the same time (repeating the set-up is
+// harmless).
 static int ensure_gemm_attrs(int dev) {
-    static int done[64] = {};
+    static std::atomic<int> done[64];
     if (dev >= 0 && dev < 64 && done[dev]) return KZ_OK;
     int st = set_smem_attr<KZ_ACT_NONE, false>();
     if (!st) st = set_smem_attr<KZ_ACT_RELU, false>();
@@ -801,7 +805,7 @@ static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const Gem
 
 // How many CTA pairs of the pair kernel can be resident at once (cached per device).
 static int max_active_pairs(int dev) {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64];
     if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));

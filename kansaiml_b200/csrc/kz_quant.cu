@@ -35,6 +35,7 @@
 // k = rint(fl64(x/scale)).  Only the elements that fail the bound (about one in
 // 16000 for smooth data) take the exact division.
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <mutex>
 
@@ -802,7 +803,7 @@ int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials
 }
 
 static int fused_grid(int dev) {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64];   // per device; first calls may race (the value is the same)
     if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_fused_kernel, 1024, 0) != cudaSuccess)
@@ -847,7 +848,7 @@ int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, 
     const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
     if (aligned) {
         // one block per SM, its chunk resident in shared memory
-        static int smem_set[64] = {};
+        static std::atomic<int> smem_set[64];
         int max_smem = 0;
         KZ_CHECK_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         const int dyn = max_smem - 1024;   // leave room for the kernel's static shared memory
