@@ -42,6 +42,8 @@ sys.path.insert(0, ROOT)
 M_TOK, K_IN, N_OUT = 2048, 4096, 4096
 NSETS = 4
 METRIC = "int8 GEMM TOPS & quantized-linear tokens/s vs int8 roofline at 1/2/4/8 B200"
+WORKLOAD = ("config2: per-channel int8 quantized Linear [4096 -> 4096], 2048 tokens/step/GPU, "
+            "per-tensor activation quant, fused rescale, fp32 out")
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
 
 
@@ -207,8 +209,9 @@ def run_reference(args):
             "steps": timed, "steps_requested": args.steps, "warmup": min(args.warmup, 1), "ms_per_step": dt * 1e3,
             "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config2 per-channel int8 Linear [4096x4096] @ 2048 tokens (reference: W8A32 per-tensor)",
-                       "global_batch": M_TOK, "parallelism": "host threads"},
+            "config": {"workload": WORKLOAD, "global_batch": M_TOK, "parallelism": "host threads",
+                       "reference_path": "the reference's only qlinear: per-tensor int8 weight dequantized to fp32 "
+                                         "every call (quantize.py:115-122), fp32 Tensor::matmul + add"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference", "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -456,8 +459,7 @@ def main():
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "config2: per-channel int8 quantized Linear [4096 -> 4096], 2048 tokens/step/GPU, "
-                               "per-tensor activation quant, fused rescale, fp32 out",
+        "config": {"workload": WORKLOAD,
                    "launch": f"CUDA graphs of {S} steps (2 libkz kernels per step) replayed back to back",
                    "global_batch": tokens, "seq_len": None, "parallelism": f"dp{world} (row-sharded activations)",
                    "l2": f"inputs larger than L2: {NSETS} rotating (X, W, Y) sets, "
