@@ -113,6 +113,16 @@ int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, 
 int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
                               float* y, uint32_t* partials, kz_stream_t stream);
 
+/* kz_layernorm_partials_f32 of x + res, with the sum also written to sum_out:
+ * a pre-LN block's residual connection (nn.py:476-477, x = x.add(...))
+ * folded into the LayerNorm that follows it.  Each element of the sum is one
+ * fp32 add, rounded as the reference's Tensor::add rounds it, so sum_out and
+ * y equal the unfused x.add(res) followed by kz_layernorm_partials_f32 bit for
+ * bit.  sum_out must not alias x, res or y. */
+int kz_add_layernorm_partials_f32(const float* x, const float* res, int64_t M, int64_t D, const float* gamma,
+                                  const float* beta, float eps, float* sum_out, float* y, uint32_t* partials,
+                                  kz_stream_t stream);
+
 /* Per-output-channel quantize of a reference-layout weight w[K, N] (row-major,
  * nn.py:74-81: [in_features, out_features]); channel n is column n.  Writes
  * K-major codes qT[N, K], scales[N] (double) and scales_f32[N].  Each column

@@ -555,11 +555,17 @@ __device__ __forceinline__ float warp_sum_f32(float v) {
 // y = (x - mean) / sqrt(var + eps) * gamma + beta), one warp per row, writing
 // y and the absmax partials of y (block b -> partials[1 + b]) so that
 // kz_quantize_partials_f32 can quantize y per tensor without another pass.
+// With `res` (a residual of x's shape), the row normalised is x + res, one
+// fp32 add per element as torch's add rounds it, and `sum_out` receives it:
+// the residual connection of a pre-LN block folded into the LayerNorm that
+// follows it (nn.py:476-477).
 __global__ void __launch_bounds__(256) layernorm_partials_kernel(const float* __restrict__ x, int64_t M, int64_t D,
                                                                  const float* __restrict__ gamma,
                                                                  const float* __restrict__ beta, float eps,
                                                                  float* __restrict__ y,
-                                                                 uint32_t* __restrict__ partials) {
+                                                                 uint32_t* __restrict__ partials,
+                                                                 const float* __restrict__ res,
+                                                                 float* __restrict__ sum_out) {
     griddep_launch_dependents();
     griddep_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -567,18 +573,23 @@ __global__ void __launch_bounds__(256) layernorm_partials_kernel(const float* __
     uint32_t m = 0;
     for (int64_t r = blockIdx.x * 8 + warp; r < M; r += (int64_t)gridDim.x * 8) {
         const float* xr = x + r * D;
+        const float* rr = res ? res + r * D : nullptr;
+        auto val = [&](int64_t j) { return rr ? __fadd_rn(xr[j], rr[j]) : xr[j]; };
         float s = 0.0f;
-        for (int64_t j = lane; j < D; j += 32) s = __fadd_rn(s, xr[j]);
+        for (int64_t j = lane; j < D; j += 32) s = __fadd_rn(s, val(j));
         const float mean = __fmul_rn(warp_sum_f32(s), inv_d);
         float v = 0.0f;
         for (int64_t j = lane; j < D; j += 32) {
-            const float c = __fsub_rn(xr[j], mean);
+            const float c = __fsub_rn(val(j), mean);
             v = __fadd_rn(v, __fmul_rn(c, c));
         }
         const float den = __fsqrt_rn(__fadd_rn(__fmul_rn(warp_sum_f32(v), inv_d), eps));
         float* yr = y + r * D;
+        float* sr = sum_out ? sum_out + r * D : nullptr;
         for (int64_t j = lane; j < D; j += 32) {
-            float o = __fdiv_rn(__fsub_rn(xr[j], mean), den);
+            const float xv = val(j);
+            if (sr) sr[j] = xv;
+            float o = __fdiv_rn(__fsub_rn(xv, mean), den);
             if (gamma) o = __fmul_rn(o, gamma[j]);
             if (beta) o = __fadd_rn(o, beta[j]);
             yr[j] = o;
@@ -814,8 +825,9 @@ static int fused_grid(int dev) {
     return g;
 }
 
-int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
-                              float* y, uint32_t* partials, kz_stream_t stream) {
+static int layernorm_partials_impl(const float* x, const float* res, int64_t M, int64_t D, const float* gamma,
+                                   const float* beta, float eps, float* sum_out, float* y, uint32_t* partials,
+                                   kz_stream_t stream) {
     KZ_REQUIRE(M >= 0 && D > 0, "kz_layernorm_partials_f32: need M >= 0 and D > 0");
     KZ_REQUIRE(partials, "kz_layernorm_partials_f32: partials is NULL");
     KZ_REQUIRE(M == 0 || (x && y), "kz_layernorm_partials_f32: x or y is NULL");
@@ -825,8 +837,22 @@ int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float*
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, cap));
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     KZ_CHECK_CUDA(launch_pdl(layernorm_partials_kernel, dim3(grid), dim3(256), 0, s, x, M, D, gamma, beta, eps, y,
-                             partials));
+                             partials, res, sum_out));
     return KZ_OK;
+}
+
+int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
+                              float* y, uint32_t* partials, kz_stream_t stream) {
+    return layernorm_partials_impl(x, nullptr, M, D, gamma, beta, eps, nullptr, y, partials, stream);
+}
+
+int kz_add_layernorm_partials_f32(const float* x, const float* res, int64_t M, int64_t D, const float* gamma,
+                                  const float* beta, float eps, float* sum_out, float* y, uint32_t* partials,
+                                  kz_stream_t stream) {
+    KZ_REQUIRE(M == 0 || (res && sum_out), "kz_add_layernorm_partials_f32: res or sum_out is NULL");
+    KZ_REQUIRE(M == 0 || (sum_out != x && sum_out != res && sum_out != y),
+               "kz_add_layernorm_partials_f32: sum_out must not alias x, res or y");
+    return layernorm_partials_impl(x, res, M, D, gamma, beta, eps, sum_out, y, partials, stream);
 }
 
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,

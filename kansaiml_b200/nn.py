@@ -216,10 +216,14 @@ class TransformerBlock(Module):
         self.fc2 = QLinear(self.fc2, per_channel=per_channel, activations=activations)
         return self
 
+    def _w8a8(self):
+        return isinstance(self.fc1, QLinear) and self.attn.qkv is not None
+
     def forward(self, x, mask=None):
         x = as_tensor(x)
-        if isinstance(self.fc1, QLinear) and self.attn.qkv is not None:
-            return self._forward_w8a8(x, mask)
+        if self._w8a8():
+            x, pending = self._forward_w8a8(x, mask)
+            return x.add(pending)
         normed = self.ln1(x)
         x = x.add(self.attn(normed, normed, normed, mask=mask))
         h = self.ln2(x)
@@ -229,18 +233,24 @@ class TransformerBlock(Module):
             h = self.gelu(self.fc1(h))
         return x.add(self.fc2(h))
 
-    def _forward_w8a8(self, x, mask):
+    def _forward_w8a8(self, x, mask, pending=None):
         """The same block with every activation quantized where it is made:
         LayerNorm -> quantize is one LayerNorm kernel (with the absmax) plus
         one quantize pass; fc1's GEMM epilogue (bias + GELU) also emits the
-        absmax of its output, so fc2's input is quantized in one pass."""
+        absmax of its output, so fc2's input is quantized in one pass.  The
+        residual adds are folded into the LayerNorm that follows each one: the
+        block's input is x + pending (pending None: x), and it returns
+        (x, pending) with its output x + pending, for the next LayerNorm to
+        add."""
         ln1, ln2 = self.ln1, self.ln2
-        qa = QActivation.layernorm(x, ln1.weight, ln1.bias, ln1.eps)
-        x = x.add(self.attn(qa, qa, qa, mask=mask))
-        qb = QActivation.layernorm(x, ln2.weight, ln2.bias, ln2.eps)
+        if pending is None:
+            qa = QActivation.layernorm(x, ln1.weight, ln1.bias, ln1.eps)
+        else:
+            x, qa = QActivation.add_layernorm(x, pending, ln1.weight, ln1.bias, ln1.eps)
+        x, qb = QActivation.add_layernorm(x, self.attn(qa, qa, qa, mask=mask), ln2.weight, ln2.bias, ln2.eps)
         partials = partials_buffer(x.data.device)
         h = self.fc1(qb, act="gelu", out_partials=partials)
-        return x.add(self.fc2(QActivation.from_partials(h, partials)))
+        return x, self.fc2(QActivation.from_partials(h, partials))
 
 
 class CausalMask(Tensor):

@@ -90,10 +90,12 @@ def quantize_partials_device(x, partials):
     return q, s64, s32
 
 
-def layernorm_partials_device(x, weight=None, bias=None, eps=1e-5, partials=None):
+def layernorm_partials_device(x, weight=None, bias=None, eps=1e-5, partials=None, residual=None):
     """LayerNorm over the last axis of a contiguous fp32 CUDA tensor, plus the
-    absmax partials of the result (kz_layernorm_partials_f32).
-    Returns (y, partials)."""
+    absmax partials of the result (kz_layernorm_partials_f32).  With
+    `residual` (same shape), the LayerNorm of x + residual, the sum returned
+    too (kz_add_layernorm_partials_f32).  Returns (y, partials) or
+    (y, partials, x + residual)."""
     dev = x.device
     D = x.shape[-1]
     M = x.numel() // D
@@ -102,9 +104,16 @@ def layernorm_partials_device(x, weight=None, bias=None, eps=1e-5, partials=None
     y = torch.empty(x.shape, dtype=torch.float32, device=dev)
     w = _dev_tensor(weight, "layernorm weight") if weight is not None else None
     b = _dev_tensor(bias, "layernorm bias") if bias is not None else None
-    _lib.call("kz_layernorm_partials_f32", ptr(x), M, D, ptr(w), ptr(b), float(eps), ptr(y), ptr(partials),
-              stream_handle(dev))
-    return y, partials
+    if residual is None:
+        _lib.call("kz_layernorm_partials_f32", ptr(x), M, D, ptr(w), ptr(b), float(eps), ptr(y), ptr(partials),
+                  stream_handle(dev))
+        return y, partials
+    if tuple(residual.shape) != tuple(x.shape):
+        raise ValueError(f"add_layernorm: residual shape {list(residual.shape)} != {list(x.shape)}")
+    total = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    _lib.call("kz_add_layernorm_partials_f32", ptr(x), ptr(residual), M, D, ptr(w), ptr(b), float(eps), ptr(total),
+              ptr(y), ptr(partials), stream_handle(dev))
+    return y, partials, total
 
 
 def absmax_partials_device(x, partials=None):
@@ -212,6 +221,15 @@ class QActivation:
         kernel emits the absmax partials, so the quantize is a single pass."""
         y, partials = layernorm_partials_device(_dev_tensor(x, "QActivation.layernorm"), weight, bias, eps)
         return cls(*quantize_partials_device(y, partials))
+
+    @classmethod
+    def add_layernorm(cls, x, residual, weight=None, bias=None, eps=1e-5):
+        """x + residual (a pre-LN block's residual connection, nn.py:476-477)
+        and the LayerNorm of that sum quantized per tensor, from one LayerNorm
+        kernel that also writes the sum.  Returns (Tensor sum, QActivation)."""
+        y, partials, total = layernorm_partials_device(_dev_tensor(x, "QActivation.add_layernorm"), weight, bias,
+                                                       eps, residual=_dev_tensor(residual, "QActivation.add_layernorm"))
+        return Tensor(total), cls(*quantize_partials_device(y, partials))
 
 
 class QTensor:

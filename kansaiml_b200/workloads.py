@@ -63,10 +63,20 @@ class Decoder(nn.Module):
         s = ids.shape[1]
         x = Tensor(self.tok.weight.data[ids] + self.pos.weight.data[:s])
         mask = self.mask if s == self.ctx else nn.CausalMask(self.mask.data[:, :, :s, :s].contiguous())
+        # each block's feed-forward residual is added inside the next LayerNorm
+        pending = None
         for blk in self.blocks:
-            x = blk(x, mask=mask)
+            if blk._w8a8():
+                x, pending = blk._forward_w8a8(x, mask, pending)
+            else:
+                x = blk(x if pending is None else x.add(pending), mask=mask)
+                pending = None
         ln = self.ln
-        return self.head(QActivation.layernorm(x, ln.weight, ln.bias, ln.eps))
+        if pending is None:
+            qa = QActivation.layernorm(x, ln.weight, ln.bias, ln.eps)
+        else:
+            _, qa = QActivation.add_layernorm(x, pending, ln.weight, ln.bias, ln.eps)
+        return self.head(qa)
 
 
 def config3_ids(batch=32, ctx=256, vocab=65, seed=0, device="cuda"):

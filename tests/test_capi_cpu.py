@@ -109,3 +109,8 @@ def test_exchange_entry_points_validate_arguments_without_gpu():
     assert lib.kz_peer_open(None, None) == 1
     assert lib.kz_layernorm_partials_f32(one, 4, 0, None, None, ctypes.c_float(1e-5), one, one, None) == 1
     assert lib.kz_layernorm_partials_f32(one, 4, 8, None, None, ctypes.c_float(1e-5), one, None, None) == 1
+    # fused residual add + LayerNorm: the residual and the sum are required, the sum may not alias an input
+    assert lib.kz_add_layernorm_partials_f32(one, None, 4, 8, None, None, ctypes.c_float(1e-5), P(32), one, one,
+                                             None) == 1 and "res or sum_out" in _lib.last_error()
+    assert lib.kz_add_layernorm_partials_f32(one, P(32), 4, 8, None, None, ctypes.c_float(1e-5), one, P(48), one,
+                                             None) == 1 and "alias" in _lib.last_error()

@@ -99,6 +99,27 @@ def test_layernorm_quantize_vs_oracle(cuda_device):
     assert (diff != 0).mean() <= 1e-3
 
 
+def test_add_layernorm_equals_add_then_layernorm(cuda_device):
+    """kz_add_layernorm_partials_f32 (the residual add folded into the
+    LayerNorm that follows it) against torch's add followed by the plain
+    LayerNorm kernel: the sum, the normalised output, the codes and the scale
+    are bit-identical."""
+    import kansaiml_b200 as kz
+    from kansaiml_b200 import quantize as kq
+    rs = np.random.RandomState(12)
+    x = (rs.standard_normal((1000, 256)) * 2).astype(np.float32)
+    r = rs.standard_normal((1000, 256)).astype(np.float32)
+    g = rs.uniform(0.5, 1.5, 256).astype(np.float32)
+    b = rs.standard_normal(256).astype(np.float32) * 0.1
+    xt, rt, gt, bt = (kz.from_numpy(a) for a in (x, r, g, b))
+    total, qa = kq.QActivation.add_layernorm(xt, rt, gt, bt, 1e-5)
+    plain_sum = xt.data + rt.data
+    y_ref, parts = kq.layernorm_partials_device(plain_sum, gt, bt, 1e-5, partials=kq.new_partials(plain_sum.device))
+    q_ref = kq.QActivation.from_partials(kz.Tensor(y_ref), parts)
+    assert torch.equal(total.data, plain_sum)
+    assert torch.equal(qa.codes, q_ref.codes) and qa.scale == q_ref.scale
+
+
 def test_causal_flag_matches_the_explicit_mask(cuda_device):
     """causal_mask() reaches attention as is_causal.  Its -1e9 entries give
     weight exactly 0 (every row keeps its own position, so the shifted
