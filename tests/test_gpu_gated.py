@@ -5,7 +5,6 @@ bit for bit.  Failure detection without a GPU fault: a flag that nothing ever
 sets makes the kernel's bounded wait (1 s) run out; the kernel records
 KZ_ERR_DEVICE_TIMEOUT in the status word and unwinds, and the context stays
 usable."""
-import numpy as np
 import pytest
 import torch
 
