@@ -99,6 +99,26 @@ def test_layernorm_quantize_vs_oracle(cuda_device):
     assert (diff != 0).mean() <= 1e-3
 
 
+def test_block_forward_matches_the_unfused_composition(model_and_ids):
+    """A quantized TransformerBlock's forward (residual adds folded into the
+    LayerNorms) equals the same block composed from separate adds and
+    LayerNorms, bit for bit."""
+    from kansaiml_b200 import quantize as kq
+    from kansaiml_b200.tensor import Tensor
+    model, ids = model_and_ids
+    blk, mask = model.blocks[0], model.mask
+    x = Tensor(model.tok.weight.data[ids] + model.pos.weight.data[: ids.shape[1]])
+    y = blk(x, mask=mask).data
+    ln1, ln2 = blk.ln1, blk.ln2
+    qa = kq.QActivation.layernorm(x, ln1.weight, ln1.bias, ln1.eps)
+    x1 = x.add(blk.attn(qa, qa, qa, mask=mask))
+    qb = kq.QActivation.layernorm(x1, ln2.weight, ln2.bias, ln2.eps)
+    parts = kq.new_partials(x.data.device)
+    h = blk.fc1(qb, act="gelu", out_partials=parts)
+    ref = x1.add(blk.fc2(kq.QActivation.from_partials(h, parts))).data
+    assert torch.equal(y, ref)
+
+
 def test_add_layernorm_equals_add_then_layernorm(cuda_device):
     """kz_add_layernorm_partials_f32 (the residual add folded into the
     LayerNorm that follows it) against torch's add followed by the plain
