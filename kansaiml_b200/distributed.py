@@ -368,6 +368,15 @@ def column_shard_bounds(total, rank, world):
 
 # -------------------------------------------------- config 5: sharded stack
 
+def _row_chunk(M):
+    """Rows per chunk of a gathered block: the smallest multiple of 128 that
+    divides M (M % 128 == 0) and leaves at most 8 chunks, so the first GEMM
+    tiles can start after about an eighth of each block has arrived."""
+    m128 = M // 128
+    d = next(v for v in range(-(-m128 // 8), m128 + 1) if m128 % v == 0)
+    return d * 128
+
+
 class _PeerGather:
     """Two [G][M][Kb] int8 gather buffers per rank (one per layer parity),
     exported to the other ranks through CUDA IPC.  Rank g writes block g of its
@@ -381,11 +390,8 @@ class _PeerGather:
         self.world, self.rank, self.group, self.device = world, rank, group, device
         self.block = M * kb
         self.kb = kb
-        # about 8 row chunks, each a multiple of 128 rows dividing M (M % 128 == 0)
-        m128 = M // 128
-        d = next(v for v in range(-(-m128 // 8), m128 + 1) if m128 % v == 0)
-        self.rows = d * 128
-        self.chunks = -(-M // self.rows)
+        self.rows = _row_chunk(M)
+        self.chunks = M // self.rows
         # two gather buffers (one per layer parity) and, for the fused GEMM, one
         # flags buffer per parity (ready flags the peers write, then counters)
         self.flag_words = 2 * world * self.chunks

@@ -206,3 +206,15 @@ def test_dtensor_grad_gloo_world2():
         assert res[r][1] is not None, res[r][0]
         assert res[r][0] == expect
         assert res[r][1] == (np.arange(24, dtype=np.float32) + 1).tobytes()
+
+
+def test_gather_row_chunks():
+    """The overlapped all-gather's row chunks: multiples of 128 rows that
+    divide M, at most 8 of them, and the smallest such chunk."""
+    from kansaiml_b200.distributed import _row_chunk
+    for M in [128, 256, 384, 640, 896, 1024, 1152, 1664, 8192, 128 * 13, 128 * 97]:
+        rows = _row_chunk(M)
+        assert rows % 128 == 0 and M % rows == 0 and M // rows <= 8, M
+        smaller = [r for r in range(128, rows, 128) if M % r == 0 and M // r <= 8]
+        assert not smaller, (M, rows, smaller)
+    assert _row_chunk(8192) == 1024 and _row_chunk(128 * 13) == 128 * 13
