@@ -218,3 +218,44 @@ def test_gather_row_chunks():
         smaller = [r for r in range(128, rows, 128) if M % r == 0 and M // r <= 8]
         assert not smaller, (M, rows, smaller)
     assert _row_chunk(8192) == 1024 and _row_chunk(128 * 13) == 128 * 13
+
+
+# ------------------------------------------------- properties (hypothesis)
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=300, deadline=None)
+@given(total=st.integers(0, 10 ** 6), n=st.integers(1, 64))
+def test_chunk_sizes_properties(total, n):
+    """The reference's split (distributed.py:157-159): n pieces that sum to
+    total, as equal as possible, the larger ones first."""
+    from kansaiml_b200.distributed import _chunk_sizes
+    sizes = _chunk_sizes(total, n)
+    assert len(sizes) == n and sum(sizes) == total
+    assert max(sizes) - min(sizes) <= 1
+    assert sizes == sorted(sizes, reverse=True)
+
+
+@settings(max_examples=300, deadline=None)
+@given(total=st.integers(0, 10 ** 6), world=st.integers(1, 64))
+def test_column_shard_bounds_tile_the_columns(total, world):
+    """Shard(1) column ranges of all ranks are contiguous, disjoint and cover
+    [0, total) in rank order."""
+    from kansaiml_b200.distributed import _chunk_sizes, column_shard_bounds
+    stop = 0
+    for rank, size in enumerate(_chunk_sizes(total, world)):
+        start, end = column_shard_bounds(total, rank, world)
+        assert start == stop and end - start == size
+        stop = end
+    assert stop == total
+
+
+@settings(max_examples=300, deadline=None)
+@given(m128=st.integers(1, 4096))
+def test_gather_row_chunk_properties(m128):
+    from kansaiml_b200.distributed import _row_chunk
+    M = 128 * m128
+    rows = _row_chunk(M)
+    assert rows % 128 == 0 and M % rows == 0 and M // rows <= 8
+    assert all(M % r or M // r > 8 for r in range(128, rows, 128))
