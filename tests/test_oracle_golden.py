@@ -119,3 +119,52 @@ def test_int8_gemm_and_epilogue_small():
     y = ocpu.epilogue(acc, rsc, csc)
     ref = (acc.astype(np.float32) * rsc.astype(np.float32)[:, None]).astype(np.float32) * csc.astype(np.float32)[None, :]
     assert y.tobytes() == ref.astype(np.float32).tobytes()
+
+
+# ------------------------------------------- randomized restatement check
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+def _py_quantize(x):
+    """quantize.py:66-69 verbatim in plain Python: fp32 values widened to
+    float, max |v|, scale = max / 127.0 (1.0 for all zeros), codes
+    max(-127, min(127, round(v / scale))) with Python's half-to-even round."""
+    flat = [float(v) for v in np.asarray(x, np.float32).ravel()]
+    max_abs = max((abs(v) for v in flat), default=0.0)
+    scale = max_abs / 127.0 if max_abs > 0.0 else 1.0
+    return [max(-127, min(127, round(v / scale))) for v in flat], scale
+
+
+_BIG = float(np.float32(1e30))
+_f32s = st.floats(min_value=-_BIG, max_value=_BIG, allow_nan=False, allow_infinity=False, width=32)
+
+
+@settings(max_examples=400, deadline=None)
+@given(st.lists(_f32s, min_size=1, max_size=64))
+def test_oracle_quantize_matches_plain_python(values):
+    x = np.asarray(values, np.float32)
+    q, s = ocpu.quantize_tensor(x)
+    q_py, s_py = _py_quantize(x)
+    assert s == s_py
+    assert q.tolist() == q_py
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.integers(1, 127), st.lists(st.tuples(st.integers(-127, 127), st.sampled_from([-1, 0, 1])),
+                                     min_size=1, max_size=32))
+def test_oracle_quantize_near_ties(top, steps):
+    """Values placed on and one ulp either side of (k + 1/2) * scale, where
+    round-half-even decides: the oracle's codes equal Python's."""
+    scale = top / 127.0
+    vals = [np.float32(top)]
+    for k, d in steps:
+        v = np.float32((k + 0.5) * scale)
+        if d:
+            v = np.nextafter(v, np.float32(np.inf if d > 0 else -np.inf))
+        vals.append(v)
+    x = np.asarray(vals, np.float32)
+    q, s = ocpu.quantize_tensor(x)
+    q_py, s_py = _py_quantize(x)
+    assert s == s_py
+    assert q.tolist() == q_py
