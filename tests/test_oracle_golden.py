@@ -168,3 +168,35 @@ def test_oracle_quantize_near_ties(top, steps):
     q_py, s_py = _py_quantize(x)
     assert s == s_py
     assert q.tolist() == q_py
+
+
+@settings(max_examples=200, deadline=None)
+@given(st.integers(1, 12), st.integers(1, 12), st.integers(0, 2 ** 31 - 1))
+def test_oracle_quantize_cols_is_per_column_quantize(K, N, seed):
+    """Per-output-channel quantize = quantize.py:66-69 applied to each column
+    of the [in, out] weight, codes stored K-major [N, K]."""
+    rs = np.random.RandomState(seed)
+    w = (rs.standard_normal((K, N)) * rs.uniform(1e-3, 1e3, N)).astype(np.float32)
+    w[:, rs.rand(N) < 0.1] = 0.0                       # some all-zero channels (scale 1.0)
+    qT, s = ocpu.quantize_cols(w)
+    for n in range(N):
+        q_py, s_py = _py_quantize(w[:, n])
+        assert s[n] == s_py
+        assert qT[n].tolist() == q_py
+
+
+@settings(max_examples=200, deadline=None)
+@given(st.integers(1, 8), st.integers(1, 8), st.booleans(), st.booleans(), st.integers(0, 2 ** 31 - 1))
+def test_oracle_epilogue_is_fp32_arithmetic(M, N, per_row, with_bias, seed):
+    """The W8A8 epilogue y = ((float)acc * row_scale) * col_scale (+ bias),
+    each step one fp32 rounding, as numpy's float32 operations give it."""
+    rs = np.random.RandomState(seed)
+    acc = rs.randint(-2 ** 31 + 1, 2 ** 31 - 1, (M, N), dtype=np.int64).astype(np.int32)
+    row = rs.uniform(1e-4, 1e-1, M if per_row else 1)
+    col = rs.uniform(1e-4, 1e-1, N)
+    bias = rs.standard_normal(N).astype(np.float32) if with_bias else None
+    y = ocpu.epilogue(acc, row if per_row else row[0], col, bias)
+    ref = (acc.astype(np.float32) * row.astype(np.float32).reshape(-1, 1)) * col.astype(np.float32)
+    if with_bias:
+        ref = ref + bias
+    assert y.tobytes() == ref.astype(np.float32).tobytes()
