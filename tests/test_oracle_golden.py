@@ -200,3 +200,37 @@ def test_oracle_epilogue_is_fp32_arithmetic(M, N, per_row, with_bias, seed):
     if with_bias:
         ref = ref + bias
     assert y.tobytes() == ref.astype(np.float32).tobytes()
+
+
+@settings(max_examples=150, deadline=None)
+@given(st.integers(1, 9), st.integers(1, 9), st.integers(1, 200), st.integers(0, 2 ** 31 - 1))
+def test_oracle_gemm_i8_is_exact_integer_matmul(M, N, K, seed):
+    rs = np.random.RandomState(seed)
+    a = rs.randint(-128, 128, (M, K)).astype(np.int8)
+    b = rs.randint(-128, 128, (N, K)).astype(np.int8)
+    acc = ocpu.gemm_i8(a, b)
+    assert np.array_equal(acc, (a.astype(np.int64) @ b.astype(np.int64).T).astype(np.int32))
+
+
+@settings(max_examples=60, deadline=None)
+@given(st.integers(1, 4), st.integers(1, 4), st.integers(1, 40), st.booleans(), st.integers(0, 2 ** 31 - 1))
+def test_oracle_qlinear_w8a32_is_the_k_ordered_loop(M, N, K, relu, seed):
+    """quantize.py:115-122 on Linux: the weight dequantized to fp32
+    (fl32(fl64(q) * scale)), then Ops.cpp's loop: every out[i, j] summed in
+    k order with each product and each sum rounded to fp32, bias, ReLU."""
+    rs = np.random.RandomState(seed)
+    x = rs.standard_normal((M, K)).astype(np.float32)
+    q = rs.randint(-127, 128, (K, N)).astype(np.int8)
+    scale = float(rs.uniform(1e-3, 1e-1))
+    bias = rs.standard_normal(N).astype(np.float32)
+    y = ocpu.qlinear_w8a32(x, q, scale, bias, act=1 if relu else 0)
+    w = (q.astype(np.float64) * scale).astype(np.float32)
+    ref = np.empty((M, N), np.float32)
+    for i in range(M):
+        for j in range(N):
+            acc = np.float32(0.0)
+            for k in range(K):
+                acc = np.float32(acc + np.float32(x[i, k] * w[k, j]))
+            v = np.float32(acc + bias[j])
+            ref[i, j] = (v if v > 0 else np.float32(0.0)) if relu else v   # x > 0 ? x : 0, as Ops.cpp
+    assert y.tobytes() == ref.tobytes()
