@@ -10,7 +10,8 @@
  * Each entry point names the reference interface it replaces
  * (reference file:line, paths inside the KansaiML checkout).  The reference
  * reaches all of them through its `kansai._core` extension
- * (python/bindings.cpp:17); INTEGRATION.md shows the binding.
+ * (python/bindings.cpp:17), which gains one thin wrapper per entry point
+ * (GIL released, non-zero status raised as RuntimeError).
  *
  * Memory: the library allocates no device memory.  Outputs, and the small
  * `partials` buffers some entry points use to hand an absmax from one kernel
@@ -19,6 +20,11 @@
  * Errors found on the device (a NaN/Inf in a tensor being quantized, a wait
  * inside a kernel that ran out) cannot be returned synchronously; kernels
  * record them in a sticky per-device status word read by kz_device_status().
+ *
+ * Per-device state (the status word's device address, the static scratch of
+ * kz_quantize_cols_f32_noalloc) is resolved on the first call on each device
+ * and cached for the life of the process.  cudaDeviceReset ends the context
+ * that state lives in: do not call libkz on a device after resetting it.
  */
 #ifndef KZ_H_
 #define KZ_H_
@@ -103,13 +109,19 @@ int kz_quantize_partials_f32(const float* x, int64_t n, const uint32_t* partials
 int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, float* scale_f32,
                            uint32_t* partials, kz_stream_t stream);
 
-/* LayerNorm over the last axis of x[M, D] (nn.py:308-331: mean, biased
- * variance, eps; y = (x - mean) / sqrt(var + eps) * gamma + beta, gamma/beta
- * may be NULL for 1/0), writing y[M, D] and the absmax partials of y in the
- * KZ_PARTIALS_WORDS format, so kz_quantize_partials_f32 quantizes y per tensor
- * without another pass over it: the prologue of a quantized Linear that
- * follows a LayerNorm.  No reference counterpart (the reference runs
- * LayerNorm and quantize_symmetric separately).  fp32 throughout. */
+/* LayerNorm over the last axis of x[M, D] in the reference's operation order
+ * (nn.py:323-331): mean = sum(dim) * fl32(1/D), with sum(dim) adding each
+ * row's elements one by one in index order (Tensor.cpp:831-880 ->
+ * backend/cpu/src/Ops.cpp:157-190); centered = x - mean; var = the same
+ * ordered sum of centered * centered times fl32(1/D); y = centered *
+ * fl32(1 / sqrt(var + eps)) * gamma + beta (Tensor::div multiplies by the
+ * reciprocal, Tensor.cpp:677-679); every step one fp32 operation rounded to
+ * nearest, so y equals the reference's LayerNorm bit for bit.  gamma / beta
+ * may be NULL: ones / zeros, the reference's initial parameters.  Also writes
+ * the absmax partials of y in the KZ_PARTIALS_WORDS format, so
+ * kz_quantize_partials_f32 quantizes y per tensor without another pass over
+ * it: the prologue of a quantized Linear that follows a LayerNorm (the
+ * reference runs LayerNorm and quantize_symmetric separately). */
 int kz_layernorm_partials_f32(const float* x, int64_t M, int64_t D, const float* gamma, const float* beta, float eps,
                               float* y, uint32_t* partials, kz_stream_t stream);
 

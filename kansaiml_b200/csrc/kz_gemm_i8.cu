@@ -16,8 +16,9 @@
 //          stages, tcgen05.mma.cta_group::1 M128 N256 K32); used when M <= 128.
 // Roles: warp 0 TMA producer; warp 1 TMEM allocation (512 columns = two
 // accumulators) and, in the leader, the MMA issue (one lane) with commits back
-// to both CTAs' stage barriers and accumulator barriers; warps 2..5 epilogue:
-// tcgen05.ld 32 columns at a time (each warp owns the 32 TMEM lanes of its
+// to both CTAs' stage barriers and accumulator barriers; warps 2..9 epilogue
+// (two warps per TMEM lane quarter, each draining half of the tile's columns):
+// tcgen05.ld 32 columns at a time (each warp reads the 32 TMEM lanes of its
 // sub-partition), fp32 rescale / bias / activation with the tile's column
 // scales staged in shared memory, 128B-swizzled staging and a
 // cp.async.bulk.tensor store per 32 x 32 sub-tile.  The second accumulator
@@ -958,7 +959,8 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
     }
     if (grid > KZ_PARTIALS_WORDS - 3 - p.copy_ctas) grid = (KZ_PARTIALS_WORDS - 3 - p.copy_ctas) & ~1;
     if (peers) {
-        // fused all-gather: peer tensor maps, copy CTAs in front of the computing pairs
+        // fused all-gather: the peers' buffer and flag pointers, copy CTAs in
+        // front of the computing pairs
         KZ_REQUIRE(pair && act == KZ_ACT_NONE, "kz_gemm_i8_allgather: needs M > 128 and act none");
         PeerMaps pm;
         memset(&pm, 0, sizeof(pm));

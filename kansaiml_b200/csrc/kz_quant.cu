@@ -545,64 +545,142 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
 
 // ------------------------------------------- LayerNorm with absmax partials
 
-__device__ __forceinline__ float warp_sum_f32(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
+// LayerNorm over the last axis in the reference's operation order
+// (nn.py:323-331):
+//   mean = sum(dim) * fl32(1/D)          sum(dim): Ops.cpp:157-190 reduce_to_shape
+//                                        adds the row's elements one at a time
+//                                        in index order, from 0.0f; the scale is
+//                                        a broadcast fp32 mul (Tensor.cpp:864-880)
+//   centered = x - mean
+//   var = sum(dim)(centered * centered) * fl32(1/D)
+//   y = centered * fl32(1 / sqrt(var + eps)) * gamma + beta
+//                                        (Tensor::div is mul by reciprocal,
+//                                        Tensor.cpp:677-679)
+// every step one fp32 operation rounded to nearest (the reference's x86-64
+// build has no fused multiply-add), so y equals the reference's LayerNorm bit
+// for bit.  NULL gamma / beta act as the reference's initial ones / zeros
+// (the + 0.0f still turns a -0.0 into +0.0, as the reference's add does).
+//
+// A block owns kLnRows rows.  Staged form (D % 4 == 0, 16-byte aligned rows,
+// kLnRows rows fit in shared memory): all threads copy the rows in with
+// coalesced 16-byte loads (adding the residual and writing the sum when there
+// is one), then lane r of warp 0 walks row r serially from shared memory --
+// the sums must run in index order, and one thread per row keeps the order
+// without a cross-lane combine -- reading 16 bytes at a time (the row pitch
+// is 16 bytes times an odd number modulo 128, so the eight lanes of each
+// quarter-warp hit distinct bank groups), and finally all threads write y with
+// coalesced 16-byte stores and take its absmax.  Otherwise the same
+// arithmetic reads global memory directly.
+constexpr int kLnRows = 32;
+constexpr int kLnThreads = 256;
 
-// LayerNorm over the last axis (nn.py:308-331: mean, biased variance, eps;
-// y = (x - mean) / sqrt(var + eps) * gamma + beta), one warp per row, writing
-// y and the absmax partials of y (block b -> partials[1 + b]) so that
-// kz_quantize_partials_f32 can quantize y per tensor without another pass.
-// With `res` (a residual of x's shape), the row normalised is x + res, one
-// fp32 add per element as torch's add rounds it, and `sum_out` receives it:
-// the residual connection of a pre-LN block folded into the LayerNorm that
-// follows it (nn.py:476-477).
-__global__ void __launch_bounds__(256) layernorm_partials_kernel(const float* __restrict__ x, int64_t M, int64_t D,
-                                                                 const float* __restrict__ gamma,
-                                                                 const float* __restrict__ beta, float eps,
-                                                                 float* __restrict__ y,
-                                                                 uint32_t* __restrict__ partials,
-                                                                 const float* __restrict__ res,
-                                                                 float* __restrict__ sum_out) {
+__global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
+    const float* __restrict__ x, int64_t M, int64_t D, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, float* __restrict__ y, uint32_t* __restrict__ partials,
+    const float* __restrict__ res, float* __restrict__ sum_out, int staged, int stride) {
+    extern __shared__ __align__(16) float ln_rows[];
+    __shared__ float s_mean[kLnRows], s_rden[kLnRows];
+    __shared__ uint32_t red[kLnThreads / 32];
     griddep_launch_dependents();
     griddep_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float inv_d = __frcp_rn((float)D);
+    const int64_t D4 = D >> 2;
     uint32_t m = 0;
-    for (int64_t r = blockIdx.x * 8 + warp; r < M; r += (int64_t)gridDim.x * 8) {
-        const float* xr = x + r * D;
-        const float* rr = res ? res + r * D : nullptr;
-        auto val = [&](int64_t j) { return rr ? __fadd_rn(xr[j], rr[j]) : xr[j]; };
-        float s = 0.0f;
-        for (int64_t j = lane; j < D; j += 32) s = __fadd_rn(s, val(j));
-        const float mean = __fmul_rn(warp_sum_f32(s), inv_d);
-        float v = 0.0f;
-        for (int64_t j = lane; j < D; j += 32) {
-            const float c = __fsub_rn(val(j), mean);
-            v = __fadd_rn(v, __fmul_rn(c, c));
-        }
-        const float den = __fsqrt_rn(__fadd_rn(__fmul_rn(warp_sum_f32(v), inv_d), eps));
-        float* yr = y + r * D;
-        float* sr = sum_out ? sum_out + r * D : nullptr;
-        for (int64_t j = lane; j < D; j += 32) {
-            const float xv = val(j);
-            if (sr) sr[j] = xv;
-            float o = __fdiv_rn(__fsub_rn(xv, mean), den);
-            if (gamma) o = __fmul_rn(o, gamma[j]);
-            if (beta) o = __fadd_rn(o, beta[j]);
-            yr[j] = o;
-            m = max(m, abs_bits(o));
+    for (int64_t r0 = (int64_t)blockIdx.x * kLnRows; r0 < M; r0 += (int64_t)gridDim.x * kLnRows) {
+        const int rows = (int)min((int64_t)kLnRows, M - r0);
+        if (staged) {
+            // rows in: ln_rows[r * stride + j] = x (+ res)
+            for (int64_t t = threadIdx.x; t < rows * D4; t += kLnThreads) {
+                const int r = (int)(t / D4);
+                const int64_t c = t - r * D4;
+                const int64_t g = (r0 + r) * D4 + c;
+                float4 v = __ldg(reinterpret_cast<const float4*>(x) + g);
+                if (res) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(res) + g);
+                    v.x = __fadd_rn(v.x, w.x);
+                    v.y = __fadd_rn(v.y, w.y);
+                    v.z = __fadd_rn(v.z, w.z);
+                    v.w = __fadd_rn(v.w, w.w);
+                    reinterpret_cast<float4*>(sum_out)[g] = v;
+                }
+                *reinterpret_cast<float4*>(ln_rows + (int64_t)r * stride + 4 * c) = v;
+            }
+            __syncthreads();
+            if (warp == 0 && lane < rows) {
+                const float4* row = reinterpret_cast<const float4*>(ln_rows + (int64_t)lane * stride);
+                float s = 0.0f;
+                for (int64_t c = 0; c < D4; ++c) {
+                    const float4 v = row[c];
+                    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+                }
+                const float mean = __fmul_rn(s, inv_d);
+                float q = 0.0f;
+                for (int64_t c = 0; c < D4; ++c) {
+                    const float4 v = row[c];
+                    const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean);
+                    const float e = __fsub_rn(v.z, mean), f = __fsub_rn(v.w, mean);
+                    q = __fadd_rn(q, __fmul_rn(a, a));
+                    q = __fadd_rn(q, __fmul_rn(b, b));
+                    q = __fadd_rn(q, __fmul_rn(e, e));
+                    q = __fadd_rn(q, __fmul_rn(f, f));
+                }
+                s_mean[lane] = mean;
+                s_rden[lane] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(q, inv_d), eps)));
+            }
+            __syncthreads();
+            for (int64_t t = threadIdx.x; t < rows * D4; t += kLnThreads) {
+                const int r = (int)(t / D4);
+                const int64_t c = t - r * D4;
+                const float mean = s_mean[r], rden = s_rden[r];
+                const float4 v = *reinterpret_cast<const float4*>(ln_rows + (int64_t)r * stride + 4 * c);
+                const float4 gm = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+                const float4 bt = beta ? __ldg(reinterpret_cast<const float4*>(beta) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 o;
+                o.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mean), rden), gm.x), bt.x);
+                o.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mean), rden), gm.y), bt.y);
+                o.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mean), rden), gm.z), bt.z);
+                o.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mean), rden), gm.w), bt.w);
+                reinterpret_cast<float4*>(y)[(r0 + r) * D4 + c] = o;
+                m = max(m, max(max(abs_bits(o.x), abs_bits(o.y)), max(abs_bits(o.z), abs_bits(o.w))));
+            }
+            __syncthreads();   // ln_rows and the row statistics are reused by the next row group
+        } else {
+            auto val = [&](int64_t i) { return res ? __fadd_rn(x[i], res[i]) : x[i]; };
+            if (warp == 0 && lane < rows) {
+                const int64_t base = (r0 + lane) * D;
+                float s = 0.0f;
+                for (int64_t j = 0; j < D; ++j) s = __fadd_rn(s, val(base + j));
+                const float mean = __fmul_rn(s, inv_d);
+                float q = 0.0f;
+                for (int64_t j = 0; j < D; ++j) {
+                    const float a = __fsub_rn(val(base + j), mean);
+                    q = __fadd_rn(q, __fmul_rn(a, a));
+                }
+                s_mean[lane] = mean;
+                s_rden[lane] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(q, inv_d), eps)));
+            }
+            __syncthreads();
+            for (int64_t t = threadIdx.x; t < rows * D; t += kLnThreads) {
+                const int r = (int)(t / D);
+                const int64_t j = t - r * D;
+                const int64_t i = (r0 + r) * D + j;
+                const float v = val(i);
+                if (res) sum_out[i] = v;
+                const float gm = gamma ? gamma[j] : 1.0f, bt = beta ? beta[j] : 0.0f;
+                const float o = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, s_mean[r]), s_rden[r]), gm), bt);
+                y[i] = o;
+                m = max(m, abs_bits(o));
+            }
+            __syncthreads();
         }
     }
     m = warp_max_u32(m);
-    __shared__ uint32_t red[8];
     if (lane == 0) red[warp] = m;
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t v = 0;
-        for (int w = 0; w < 8; ++w) v = max(v, red[w]);
+        for (int w = 0; w < kLnThreads / 32; ++w) v = max(v, red[w]);
         partials[1 + blockIdx.x] = v;
         if (blockIdx.x == 0) partials[0] = gridDim.x;
     }
@@ -675,6 +753,103 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(const float* __restr
         } else {
             for (int j = 0; j < 16 && kb + j < K; ++j) dst[j] = tile[row][chunk * 16 + j];
         }
+    }
+}
+
+// Vectorised forms for the common case (N % 4 == 0, K % 16 == 0, 16-byte
+// aligned w and qT).  A block is 256 threads over a tile of 64 columns: thread
+// t owns columns n0 + 4 (t % 16) .. + 3 (one 16-byte load per row) and 16
+// consecutive rows starting at 16 (t / 16), so a warp reads two 256-byte row
+// segments per load and every thread has 16 independent 16-byte loads in
+// flight.
+constexpr int kColTile = 64;
+constexpr int kColRowsPerThread = 16;
+constexpr int kColRowsPerPass = 16 * kColRowsPerThread;   // 256 rows per block pass
+
+// partial[split][n] = max |w[k][n]| over the split's rows (bit patterns).
+__global__ void __launch_bounds__(256) absmax_cols4_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                                           int64_t rows_per_split, uint32_t* __restrict__ partial) {
+    __shared__ uint32_t red[16][kColTile + 1];
+    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    const int64_t n = (int64_t)blockIdx.x * kColTile + 4 * cg;
+    const int64_t k0 = blockIdx.y * rows_per_split;
+    const int64_t k1 = min(K, k0 + rows_per_split);
+    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+    if (n < N) {
+        for (int64_t kb = k0 + rg * kColRowsPerThread; kb < k1; kb += kColRowsPerPass) {
+            float4 v[kColRowsPerThread];
+#pragma unroll
+            for (int i = 0; i < kColRowsPerThread; ++i)
+                v[i] = kb + i < k1 ? __ldg(reinterpret_cast<const float4*>(w + (kb + i) * N + n))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < kColRowsPerThread; ++i) {
+                m0 = max(m0, abs_bits(v[i].x));
+                m1 = max(m1, abs_bits(v[i].y));
+                m2 = max(m2, abs_bits(v[i].z));
+                m3 = max(m3, abs_bits(v[i].w));
+            }
+        }
+    }
+    red[rg][4 * cg] = m0;
+    red[rg][4 * cg + 1] = m1;
+    red[rg][4 * cg + 2] = m2;
+    red[rg][4 * cg + 3] = m3;
+    __syncthreads();
+    if (threadIdx.x < kColTile) {
+        const int64_t c = (int64_t)blockIdx.x * kColTile + threadIdx.x;
+        uint32_t m = 0;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) m = max(m, red[r][threadIdx.x]);
+        if (c < N) partial[blockIdx.y * N + c] = m;
+    }
+}
+
+// Transposing quantize of 64 columns x 256 rows: each thread turns its 16
+// rows x 4 columns into four 16-byte runs of K-major codes, one per column,
+// each quantized with that column's scale (pack16: fast path + exact repair).
+__global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                                             const uint32_t* __restrict__ partial, int splits,
+                                                             int8_t* __restrict__ qT, double* scales,
+                                                             float* scales_f32, int* status) {
+    __shared__ ScaleInfo s_si[kColTile];
+    const int64_t n0 = (int64_t)blockIdx.x * kColTile;
+    if (threadIdx.x < kColTile) {
+        const int64_t n = n0 + threadIdx.x;
+        uint32_t bits = 0;
+        if (n < N)
+            for (int r = 0; r < splits; ++r) bits = max(bits, partial[r * N + n]);
+        const ScaleInfo si = scale_from_absmax_bits(bits);
+        s_si[threadIdx.x] = si;
+        if (blockIdx.y == 0 && n < N) {
+            if (si.finite) {
+                scales[n] = si.scale;
+                if (scales_f32) scales_f32[n] = __double2float_rn(si.scale);
+            } else {
+                scales[n] = __longlong_as_double(0x7FF8000000000000ll);
+                if (scales_f32) scales_f32[n] = __uint_as_float(0x7FC00000u);
+                record_status(status, KZ_ERR_NONFINITE);
+            }
+        }
+    }
+    __syncthreads();
+    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    const int64_t n = n0 + 4 * cg;
+    const int64_t k = (int64_t)blockIdx.y * kColRowsPerPass + rg * kColRowsPerThread;
+    if (n >= N || k >= K) return;
+    float4 v[kColRowsPerThread];
+#pragma unroll
+    for (int i = 0; i < kColRowsPerThread; ++i) v[i] = __ldcs(reinterpret_cast<const float4*>(w + (k + i) * N + n));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const ScaleInfo si = s_si[4 * cg + j];
+        auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (si.finite)
+            out = pack16(make_float4(col(0), col(1), col(2), col(3)), make_float4(col(4), col(5), col(6), col(7)),
+                         make_float4(col(8), col(9), col(10), col(11)),
+                         make_float4(col(12), col(13), col(14), col(15)), si);
+        *reinterpret_cast<uint4*>(qT + (n + j) * K + k) = out;
     }
 }
 
@@ -825,6 +1000,17 @@ static int fused_grid(int dev) {
     return g;
 }
 
+// Row pitch (floats) of the staged LayerNorm: D rounded up so that the pitch
+// in bytes is 16 times an odd number modulo 128 (conflict-free 16-byte reads
+// by one lane per row).
+static int layernorm_stride(int64_t D) {
+    int64_t s = (D + 3) / 4 * 4;
+    while ((s % 32) % 8 != 4) s += 4;
+    return (int)s;
+}
+
+constexpr int kLnMaxSmem = 96 * 1024;
+
 static int layernorm_partials_impl(const float* x, const float* res, int64_t M, int64_t D, const float* gamma,
                                    const float* beta, float eps, float* sum_out, float* y, uint32_t* partials,
                                    kz_stream_t stream) {
@@ -833,11 +1019,27 @@ static int layernorm_partials_impl(const float* x, const float* res, int64_t M, 
     KZ_REQUIRE(M == 0 || (x && y), "kz_layernorm_partials_f32: x or y is NULL");
     int st = check_device();
     if (st) return st;
+    int dev = 0;
+    KZ_CHECK_CUDA(cudaGetDevice(&dev));
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                           reinterpret_cast<uintptr_t>(res) | reinterpret_cast<uintptr_t>(sum_out) |
+                           reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta);
+    const int stride = layernorm_stride(D);
+    const size_t smem = (size_t)kLnRows * stride * sizeof(float);
+    const int staged = (D % 4 == 0) && (bits & 15u) == 0 && smem <= (size_t)kLnMaxSmem;
+    if (staged && smem > 48 * 1024) {
+        static std::atomic<int> attr_set[64];
+        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+            KZ_CHECK_CUDA(cudaFuncSetAttribute(layernorm_partials_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kLnMaxSmem));
+            if (dev >= 0 && dev < 64) attr_set[dev] = 1;
+        }
+    }
     const int64_t cap = std::min<int64_t>(4 * (int64_t)sm_count(), kFusedMaxBlocks);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, cap));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((M + kLnRows - 1) / kLnRows, cap));
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    KZ_CHECK_CUDA(launch_pdl(layernorm_partials_kernel, dim3(grid), dim3(256), 0, s, x, M, D, gamma, beta, eps, y,
-                             partials, res, sum_out));
+    KZ_CHECK_CUDA(launch_pdl(layernorm_partials_kernel, dim3(grid), dim3(kLnThreads), staged ? smem : 0, s, x, M, D,
+                             gamma, beta, eps, y, partials, res, sum_out, staged, stride));
     return KZ_OK;
 }
 
@@ -921,7 +1123,17 @@ int kz_quantize_tensor_f32(const float* x, int64_t n, int8_t* q, double* scale, 
     return KZ_OK;
 }
 
-static int64_t col_splits(int64_t K, int64_t N) {
+static bool cols_vectorised(const float* w, int64_t K, int64_t N, const int8_t* qT) {
+    return K > 0 && N % 4 == 0 && K % 16 == 0 &&
+           ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(qT)) & 15u) == 0;
+}
+
+static int64_t col_splits(int64_t K, int64_t N, bool vec) {
+    if (vec) {
+        // one 256-row pass per block where that fits in 64 splits
+        int64_t want = (K + kColRowsPerPass - 1) / kColRowsPerPass;
+        return std::max<int64_t>(1, std::min<int64_t>(want, 64));
+    }
     // enough blocks to fill the GPU: ~4 waves of (N / 32) x splits
     const int64_t col_tiles = (N + 31) / 32;
     int64_t want = (4 * (int64_t)sm_count() + col_tiles - 1) / col_tiles;
@@ -932,8 +1144,44 @@ static int64_t col_splits(int64_t K, int64_t N) {
     return want;
 }
 
+// Both per-channel quantize entry points: `partial` holds at least
+// max_words words of scratch (splits x N are used).
+static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales, float* scales_f32,
+                                uint32_t* partial, int64_t max_words, cudaStream_t s, const char* who) {
+    const bool vec = cols_vectorised(w, K, N, qT);
+    int64_t splits = K == 0 ? 1 : col_splits(K, N, vec);
+    if (splits * N > max_words) splits = std::max<int64_t>(1, max_words / N);
+    KZ_REQUIRE(splits * N <= max_words, "quantize_cols: scratch smaller than N words");
+    if (K == 0) {
+        KZ_CHECK_CUDA(cudaMemsetAsync(partial, 0, (size_t)N * sizeof(uint32_t), s));
+    } else if (vec) {
+        const int64_t rows_per_split = (K + splits - 1) / splits;
+        KZ_REQUIRE((N + kColTile - 1) / kColTile < INT32_MAX, "quantize_cols: N too large");
+        absmax_cols4_kernel<<<dim3((unsigned)((N + kColTile - 1) / kColTile), (unsigned)splits), 256, 0, s>>>(
+            w, K, N, rows_per_split, partial);
+        int st = launch_status(who);
+        if (st) return st;
+        const int64_t ktiles = (K + kColRowsPerPass - 1) / kColRowsPerPass;
+        KZ_REQUIRE(ktiles < 65536, "quantize_cols: K too large");
+        quantize_cols4_kernel<<<dim3((unsigned)((N + kColTile - 1) / kColTile), (unsigned)ktiles), 256, 0, s>>>(
+            w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
+        return launch_status(who);
+    } else {
+        const int64_t rows_per_split = (K + splits - 1) / splits;
+        absmax_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)splits), dim3(32, 8), 0, s>>>(
+            w, K, N, rows_per_split, partial);
+        int st = launch_status(who);
+        if (st) return st;
+    }
+    const int64_t ktiles = K == 0 ? 1 : (K + 127) / 128;
+    KZ_REQUIRE(ktiles < 65536, "quantize_cols: K too large");
+    quantize_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)ktiles), dim3(32, 8), 0, s>>>(
+        w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
+    return launch_status(who);
+}
+
 size_t kz_quantize_cols_workspace_bytes(int64_t K, int64_t N) {
-    if (K <= 0 || N <= 0) return 0;
+    if (K < 0 || N <= 0) return 0;   // K == 0 still clears N words of partials
     return (size_t)64 * (size_t)N * sizeof(uint32_t);
 }
 
@@ -948,25 +1196,12 @@ int kz_quantize_cols_f32(const float* w, int64_t K, int64_t N, int8_t* qT, doubl
     KZ_REQUIRE(K == 0 || (w && qT), "kz_quantize_cols_f32: w or qT is NULL");
     int st = check_device();
     if (st) return st;
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const int64_t splits = K == 0 ? 1 : col_splits(K, N);
+    const int64_t splits = K == 0 ? 1 : col_splits(K, N, cols_vectorised(w, K, N, qT));
     KZ_REQUIRE(workspace != nullptr && workspace_bytes >= (size_t)splits * (size_t)N * sizeof(uint32_t),
                "kz_quantize_cols_f32: workspace smaller than kz_quantize_cols_workspace_bytes(K, N)");
-    uint32_t* partial = static_cast<uint32_t*>(workspace);
-    if (K == 0) {
-        KZ_CHECK_CUDA(cudaMemsetAsync(partial, 0, (size_t)N * sizeof(uint32_t), s));
-    } else {
-        const int64_t rows_per_split = (K + splits - 1) / splits;
-        absmax_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)splits), dim3(32, 8), 0, s>>>(
-            w, K, N, rows_per_split, partial);
-        st = launch_status("absmax_cols_kernel");
-        if (st) return st;
-    }
-    const int64_t ktiles = K == 0 ? 1 : (K + 127) / 128;
-    KZ_REQUIRE(ktiles < 65536, "kz_quantize_cols_f32: K too large");
-    quantize_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)ktiles), dim3(32, 8), 0, s>>>(
-        w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
-    return launch_status("quantize_cols_kernel");
+    return quantize_cols_launch(w, K, N, qT, scales, scales_f32, static_cast<uint32_t*>(workspace),
+                                (int64_t)(workspace_bytes / sizeof(uint32_t)), reinterpret_cast<cudaStream_t>(stream),
+                                "kz_quantize_cols_f32");
 }
 
 int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double* scales, float* scales_f32,
@@ -1077,19 +1312,6 @@ extern "C" int kz_quantize_cols_f32_noalloc(const float* w, int64_t K, int64_t N
     uint32_t* partial = nullptr;
     st = kz::noalloc_scratch(&partial);
     if (st) return st;
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int64_t splits = K == 0 ? 1 : col_splits(K, N);
-    if (splits * N > kz::kNoAllocScratchWords) splits = kz::kNoAllocScratchWords / N;
-    if (K == 0) {
-        KZ_CHECK_CUDA(cudaMemsetAsync(partial, 0, (size_t)N * sizeof(uint32_t), s));
-    } else {
-        const int64_t rows_per_split = (K + splits - 1) / splits;
-        absmax_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)splits), dim3(32, 8), 0, s>>>(
-            w, K, N, rows_per_split, partial);
-        st = launch_status("absmax_cols_kernel (noalloc)");
-        if (st) return st;
-    }
-    quantize_cols_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)ktiles), dim3(32, 8), 0, s>>>(
-        w, K, N, partial, (int)splits, qT, scales, scales_f32, device_status_ptr());
-    return launch_status("quantize_cols_kernel (noalloc)");
+    return quantize_cols_launch(w, K, N, qT, scales, scales_f32, partial, kz::kNoAllocScratchWords,
+                                reinterpret_cast<cudaStream_t>(stream), "kz_quantize_cols_f32_noalloc");
 }

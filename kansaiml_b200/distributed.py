@@ -49,7 +49,7 @@ traffic slows the computing CTAs even when nothing waits.  The default is
 ``exchange="collective"``, the NCCL all-gather.
 """
 import ctypes
-import threading
+from concurrent.futures import ThreadPoolExecutor, wait
 
 import torch
 import torch.distributed as dist
@@ -64,26 +64,19 @@ from .tensor import Tensor, as_tensor, cat
 # ------------------------------------------------------------ host helpers
 
 def _run_parallel(work_fns):
-    """distributed.py:73-102: one thread per callable, results in order, the
-    first error re-raised after every thread has finished."""
-    results = [None] * len(work_fns)
-    errors = [None] * len(work_fns)
-
-    def runner(i):
-        try:
-            results[i] = work_fns[i]()
-        except Exception as e:  # noqa: BLE001 -- re-raised below
-            errors[i] = e
-
-    threads = [threading.Thread(target=runner, args=(i,)) for i in range(len(work_fns))]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join()
-    for e in errors:
-        if e is not None:
-            raise e
-    return results
+    """Contract of distributed.py:73-102: every callable runs concurrently on
+    its own thread (libkz and torch release the GIL), the results come back
+    in input order, and if any callable raised, the earliest one's exception
+    is raised here once all of them have finished."""
+    if not work_fns:
+        return []
+    with ThreadPoolExecutor(max_workers=len(work_fns)) as pool:
+        futures = [pool.submit(fn) for fn in work_fns]
+        wait(futures)
+    failed = next((f.exception() for f in futures if f.exception() is not None), None)
+    if failed is not None:
+        raise failed
+    return [f.result() for f in futures]
 
 
 def _chunk_sizes(total, n):
@@ -93,12 +86,11 @@ def _chunk_sizes(total, n):
 
 
 def _split_tensor(tensor, dim, n):
-    sizes = _chunk_sizes(tensor.shape[dim], n)
-    pieces, offset = [], 0
-    for size in sizes:
-        pieces.append(tensor.slice(dim, offset, offset + size))
-        offset += size
-    return pieces
+    """distributed.py:162-176: n contiguous pieces along dim, sized by
+    _chunk_sizes (torch.split at those sizes, each piece copied out as
+    Tensor.slice does)."""
+    t = as_tensor(tensor).data
+    return [Tensor(p.contiguous()) for p in torch.split(t, _chunk_sizes(t.shape[dim], n), dim)]
 
 
 def _concat_tensors(tensors, dim):

@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from .quantize import QActivation, QLinear, partials_buffer
+from .quantize import QActivation, QLinear, layernorm_partials_device, partials_buffer
 from .tensor import Tensor, as_tensor, from_flat, ones, randn, zeros
 
 
@@ -93,7 +93,10 @@ class Sequential(Module):
 
 
 class LayerNorm(Module):
-    """nn.py:308-331: normalises the last axis, biased variance, eps 1e-5."""
+    """nn.py:308-331: normalises the last axis, biased variance, eps 1e-5.
+    The forward runs libkz's LayerNorm kernel, which follows the reference's
+    operation order (ordered fp32 sums, mul by the reciprocal), so the output
+    equals the reference's bit for bit."""
 
     def __init__(self, num_features, eps=1e-5, device=None):
         self.num_features = num_features
@@ -103,11 +106,10 @@ class LayerNorm(Module):
 
     def forward(self, x):
         t = as_tensor(x).data
-        mean = t.mean(-1, keepdim=True)
-        centered = t - mean
-        var = (centered * centered).mean(-1, keepdim=True)
-        normed = centered / torch.sqrt(var + self.eps)
-        return Tensor(normed * self.weight.data + self.bias.data)
+        if t.shape[-1] != self.num_features:
+            raise RuntimeError("mul: shapes are not broadcast-compatible")
+        y, _ = layernorm_partials_device(t.contiguous(), self.weight, self.bias, self.eps)
+        return Tensor(y)
 
 
 class Embedding(Module):
@@ -191,7 +193,10 @@ class MultiHeadAttention(Module):
         b, s, _ = x.shape
         h, dk = self.num_heads, self.d_k
         qkv = self.qkv(x).data.reshape(b, s, 3, h, dk).permute(2, 0, 3, 1, 4)
-        causal = getattr(mask, "causal", False)
+        # is_causal only for a causal mask of exactly this sequence length;
+        # any other mask is added to the scores as given, so a wrong-sized one
+        # fails to broadcast, as the reference's scores.add(mask) does
+        causal = getattr(mask, "causal", False) and tuple(as_tensor(mask).shape[-2:]) == (s, s)
         m = as_tensor(mask).data if mask is not None and not causal else None
         att = torch.nn.functional.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=m, is_causal=causal)
         merged = Tensor(att.transpose(1, 2).reshape(b, s, self.d_model))

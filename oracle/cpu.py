@@ -40,6 +40,7 @@ def lib():
         L.kzo_qlinear_w8a32.argtypes = [P, I64, I64, P, D, P, I64, I, P, I]
         L.kzo_gemm_i8_i32.argtypes = [P, P, P, I64, I64, I64, I]
         L.kzo_epilogue_f32.argtypes = [P, I64, I64, P, I64, P, I64, P, I, P]
+        L.kzo_layernorm_f32.argtypes = [P, P, I64, I64, P, P, ctypes.c_float, P, P]
         _lib = L
     return _lib
 
@@ -182,3 +183,19 @@ def w8a8_linear(x, w_qT, w_scales, bias=None, act=0, per_row=False, threads=None
     acc = gemm_i8(xq, w_qT, threads)
     y = epilogue(acc, xs, w_scales, bias, act)
     return y, xq, xs, acc
+
+
+def layernorm(x, gamma=None, beta=None, eps=1e-5, residual=None):
+    """The reference's LayerNorm over the last axis (nn.py:323-331, ordered
+    fp32 sums, kz_oracle.c).  With `residual`, the LayerNorm of x + residual;
+    returns y, or (y, x + residual)."""
+    x = _f32(x)
+    D = x.shape[-1]
+    M = x.size // D
+    r = _f32(residual) if residual is not None else None
+    g = _f32(gamma) if gamma is not None else None
+    b = _f32(beta) if beta is not None else None
+    y = np.empty(x.shape, np.float32)
+    total = np.empty(x.shape, np.float32) if r is not None else None
+    lib().kzo_layernorm_f32(_p(x), _p(r), M, D, _p(g), _p(b), float(np.float32(eps)), _p(total), _p(y))
+    return y if r is None else (y, total)

@@ -255,3 +255,50 @@ void kzo_epilogue_f32(const int32_t* acc, int64_t M, int64_t N, const float* row
         }
     }
 }
+
+/* ------------------------------------------------------------- LayerNorm */
+
+/* LayerNorm over the last axis of x[M, D] (optionally of x + res, with the
+ * sum written to sum_out), in the reference's operation order:
+ *   nn.py:323-331        mean(dim), sub, mul, mean(dim), add(eps), sqrt, div,
+ *                        mul(weight), add(bias), each a separate fp32 op;
+ *   Tensor.cpp:864-880   mean(dim) = sum(dim, keepdim) * fl32(1.0f / D);
+ *   Tensor.cpp:831-841 -> Ops.cpp:157-190  sum(dim): reduce_to_shape zeroes the
+ *                        output and adds the row's elements in index order;
+ *   Ops.cpp:205-207      sqrt per element (sqrtf);
+ *   Tensor.cpp:677-679   div(other) = mul(other.reciprocal()), reciprocal
+ *                        1.0f / v per element (Ops.cpp:213-215);
+ *   eps is fl32(eps), as from_flat([eps], [1]) narrows it.
+ * gamma / beta may be NULL (ones / zeros). */
+void kzo_layernorm_f32(const float* x, const float* res, int64_t M, int64_t D, const float* gamma,
+                       const float* beta, float eps, float* sum_out, float* y) {
+    const float inv_d = 1.0f / (float)D;
+    float* row = (float*)malloc((size_t)D * sizeof(float));
+    float* cen = (float*)malloc((size_t)D * sizeof(float));
+    for (int64_t m = 0; m < M; ++m) {
+        const float* xr = x + m * D;
+        for (int64_t j = 0; j < D; ++j) row[j] = res ? xr[j] + res[m * D + j] : xr[j];
+        if (res && sum_out)
+            for (int64_t j = 0; j < D; ++j) sum_out[m * D + j] = row[j];
+        float s = 0.0f;
+        for (int64_t j = 0; j < D; ++j) s += row[j];
+        const float mean = s * inv_d;
+        for (int64_t j = 0; j < D; ++j) cen[j] = row[j] - mean;
+        float q = 0.0f;
+        for (int64_t j = 0; j < D; ++j) {
+            const float sq = cen[j] * cen[j];
+            q += sq;
+        }
+        const float var = q * inv_d;
+        const float den = sqrtf(var + eps);
+        const float rden = 1.0f / den;
+        for (int64_t j = 0; j < D; ++j) {
+            float o = cen[j] * rden;
+            o = o * (gamma ? gamma[j] : 1.0f);
+            o = o + (beta ? beta[j] : 0.0f);
+            y[m * D + j] = o;
+        }
+    }
+    free(row);
+    free(cen);
+}

@@ -2,7 +2,10 @@
 
 ``import_reference_kansai()`` loads ``python/kansai`` from the reference checkout,
 unmodified, with its ``_core`` extension resolved from ``oracle/_ref`` (the
-reference's C++ core compiled by ``make -C oracle ref``).  Nothing is copied:
+reference's C++ core compiled by ``make -C oracle ref``).  It is registered
+as the package ``kansai_reference`` (its modules import each other relatively),
+so the name ``kansai`` stays free for this repository's drop-in package and
+both can be loaded in one process.  Nothing is copied:
 the package's search path lists the reference directory first and the build
 directory second.  Available only where the reference checkout exists; the GPU
 box has only ``load_reference_core()``, the compiled core on its own.
@@ -13,7 +16,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_BUILD = os.path.join(HERE, "_ref")
-REF_ROOT = os.environ.get("KZ_REFERENCE_ROOT", "/root/reference")
+REF_PACKAGE = "kansai_reference"
+# $KZ_REFERENCE_ROOT, else a checkout named `reference` beside this repository
+REF_ROOT = os.environ.get("KZ_REFERENCE_ROOT") or os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
 
 
 def reference_available() -> bool:
@@ -34,15 +39,14 @@ def load_reference_core():
 
 def import_reference_kansai():
     """The reference's ``kansai`` package (quantize, nn, distributed, optim ...)."""
-    if "kansai" in sys.modules and getattr(sys.modules["kansai"], "_kz_reference", False):
-        return sys.modules["kansai"]
+    if REF_PACKAGE in sys.modules:
+        return sys.modules[REF_PACKAGE]
     pkg_dir = os.path.join(REF_ROOT, "python", "kansai")
     if not os.path.isdir(pkg_dir):
         raise ImportError(f"reference checkout not found at {REF_ROOT}")
     spec = importlib.util.spec_from_file_location(
-        "kansai", os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir, REF_BUILD])
+        REF_PACKAGE, os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir, REF_BUILD])
     mod = importlib.util.module_from_spec(spec)
-    sys.modules["kansai"] = mod
+    sys.modules[REF_PACKAGE] = mod
     spec.loader.exec_module(mod)
-    mod._kz_reference = True
     return mod

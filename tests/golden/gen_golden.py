@@ -25,6 +25,10 @@ Fixtures:
   xor_qlinear.npz     tests/test_quantize.py:81-125: the trained XOR model and the
                       quantized model's predictions.
   chunk_cases.npz     _chunk_sizes (distributed.py:157-159) for uneven splits.
+  layernorm_cases.npz nn.LayerNorm (nn.py:308-331) with set and default
+                      parameters, of x and of x.add(residual), and the
+                      quantize_symmetric codes of the result (config 3's
+                      LayerNorm -> quantize prologue).
 """
 import os
 import sys
@@ -39,9 +43,9 @@ from oracle.refpkg import import_reference_kansai  # noqa: E402
 import inputs  # noqa: E402
 
 kansai = import_reference_kansai()
-from kansai import nn, optim  # noqa: E402
-from kansai.distributed import _chunk_sizes  # noqa: E402
-from kansai.quantize import QLinear, QTensor, dequantize, qlinear, quantize_symmetric  # noqa: E402
+from kansai_reference import nn, optim  # noqa: E402
+from kansai_reference.distributed import _chunk_sizes  # noqa: E402
+from kansai_reference.quantize import QLinear, QTensor, dequantize, qlinear, quantize_symmetric  # noqa: E402
 
 core = kansai.core
 sha = inputs.sha
@@ -165,6 +169,30 @@ def chunk_cases():
     print("chunk_cases.npz:", sizes)
 
 
+def layernorm_cases():
+    out = {}
+    for i, shape in enumerate(inputs.LAYERNORM_SHAPES):
+        x, res, gamma, beta = inputs.layernorm_inputs(i)
+        d = shape[-1]
+        ln = nn.LayerNorm(d)
+        ln.weight, ln.bias = from_np(gamma), from_np(beta)
+        plain = nn.LayerNorm(d)
+        xt = from_np(x)
+        total = xt.add(from_np(res))                  # nn.py:476-477 residual add
+        y = ln(xt)
+        out[f"c{i}__inputs_sha256"] = np.asarray(sha(x) + sha(res) + sha(gamma) + sha(beta))
+        out[f"c{i}__y"] = to_np(y)
+        out[f"c{i}__y_default"] = to_np(plain(xt))
+        out[f"c{i}__sum"] = to_np(total)
+        out[f"c{i}__y_sum"] = to_np(ln(total))
+        q, s, _ = quantize_symmetric(y)
+        out[f"c{i}__q"] = np.asarray(q, np.int8).reshape(shape)
+        out[f"c{i}__scale"] = np.float64(s)
+    out["count"] = np.int64(len(inputs.LAYERNORM_SHAPES))
+    np.savez_compressed(os.path.join(HERE, "layernorm_cases.npz"), **out)
+    print("layernorm_cases.npz:", len(inputs.LAYERNORM_SHAPES), "shapes")
+
+
 if __name__ == "__main__":
     quantize_cases()
     percol_cases()
@@ -172,3 +200,4 @@ if __name__ == "__main__":
     mlp_config1()
     xor_qlinear()
     chunk_cases()
+    layernorm_cases()

@@ -84,3 +84,19 @@ def mlp_config1_inputs():
     b1 = (np.random.RandomState(1).standard_normal(256) * 0.05).astype(np.float32)
     b2 = (np.random.RandomState(2).standard_normal(10) * 0.05).astype(np.float32)
     return x, b1, b2
+
+
+LAYERNORM_SHAPES = [(2, 48, 256), (3, 5, 100), (64, 7)]
+
+
+def layernorm_inputs(i):
+    """(x, residual, gamma, beta) for LayerNorm case i; x has a non-zero mean
+    and a spread that keeps the ordered sums away from exact arithmetic."""
+    shape = LAYERNORM_SHAPES[i]
+    d = shape[-1]
+    rs = np.random.RandomState(300 + i)
+    x = (rs.standard_normal(shape) * 3 + 1).astype(np.float32)
+    res = rs.standard_normal(shape).astype(np.float32)
+    gamma = rs.uniform(0.5, 1.5, d).astype(np.float32)
+    beta = (rs.standard_normal(d) * 0.1).astype(np.float32)
+    return x, res, gamma, beta

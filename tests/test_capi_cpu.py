@@ -72,7 +72,8 @@ def test_check_raises_with_message():
 def test_workspace_size_query():
     lib = _lib.load()
     assert lib.kz_quantize_cols_workspace_bytes(4096, 4096) >= 4 * 4096
-    assert lib.kz_quantize_cols_workspace_bytes(0, 5) == 0
+    assert lib.kz_quantize_cols_workspace_bytes(0, 5) >= 4 * 5   # K == 0 clears one word per channel
+    assert lib.kz_quantize_cols_workspace_bytes(16, 0) == 0
 
 
 def test_exchange_entry_points_validate_arguments_without_gpu():

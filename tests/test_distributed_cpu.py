@@ -143,8 +143,8 @@ def test_all_reduce_sum_matches_reference():
     if refpkg.reference_available():
         ref = refpkg.import_reference_kansai()
         import sys
-        import kansai.distributed as rdist
-        core = sys.modules["kansai._core"]
+        import kansai_reference.distributed as rdist
+        core = sys.modules["kansai_reference._core"]
         r = rdist._all_reduce_sum([core.from_flat(p.tolist(), [p.size], False) for p in parts])
         assert np.asarray(r.tolist(), np.float32).tobytes() == ours.tobytes()
         assert ref is not None

@@ -91,7 +91,8 @@ def _spmd_worker(rank, world, port, q, exchange):
 def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
     """Two ranks over NCCL: the plain all-gather; the all-gather overlapped
     with the next GEMM (peer buffers + copy engines + the gated GEMM); and the
-    all-gather inside the GEMM launch (copy CTAs pulling peer blocks by TMA)."""
+    all-gather inside the GEMM launch (copy CTAs TMA-load this rank's block
+    from local memory and push it to the peers with 16-byte stores)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

@@ -74,3 +74,22 @@ def test_causal_mask_values_and_marker():
     want = np.triu(np.full((5, 5), -1e9, np.float32), 1)
     np.testing.assert_array_equal(np.asarray(m.tolist(), np.float32).reshape(5, 5), want)
     assert not getattr(kz.Tensor(m.data.clone()), "causal", False)
+
+
+def test_kansai_import_path_is_this_backend():
+    """The reference's import lines (tests/test_quantize.py:22-23 style) resolve
+    to this backend's objects, and both packages load side by side with the
+    reference's own (registered under another name by the oracle)."""
+    import kansai
+    from kansai.quantize import QLinear, QTensor, dequantize, qlinear, quantize_symmetric
+    from kansai import nn
+    import kansai.distributed as kdist
+    import kansaiml_b200.quantize as impl
+    assert QLinear is impl.QLinear and QTensor is impl.QTensor and qlinear is impl.qlinear
+    assert quantize_symmetric is impl.quantize_symmetric and dequantize is impl.dequantize
+    assert nn is kz.nn and kdist is kz.distributed and kansai.Tensor is kz.Tensor
+    t = kansai.tensor([[0, 1], [1, 0]], device="cpu")
+    c = kansai.tensor([[1, 0], [0, 1]], device="cpu")
+    assert kansai.where(c, t, kansai.zeros([2, 2], device="cpu")).tolist() == [0.0, 0.0, 0.0, 0.0]
+    with kansai.no_grad():
+        assert t.shape == [2, 2]

@@ -108,6 +108,26 @@ def test_xor_qlinear_vs_reference():
     assert [round(float(v)) for v in y.ravel()] == [0, 1, 1, 0]
 
 
+def test_layernorm_bit_exact_vs_reference():
+    """The oracle's LayerNorm (kz_oracle.c) against the reference's own
+    nn.LayerNorm (nn.py:323-331): with set and default parameters, of x and of
+    the residual sum x.add(res), and the quantize_symmetric codes of the
+    result -- all bit for bit."""
+    g = golden("layernorm_cases.npz")
+    for i in range(int(g["count"])):
+        x, res, gamma, beta = inputs.layernorm_inputs(i)
+        assert inputs.sha(x) + inputs.sha(res) + inputs.sha(gamma) + inputs.sha(beta) == str(g[f"c{i}__inputs_sha256"])
+        y = ocpu.layernorm(x, gamma, beta, 1e-5)
+        assert y.tobytes() == g[f"c{i}__y"].tobytes(), i
+        assert ocpu.layernorm(x).tobytes() == g[f"c{i}__y_default"].tobytes(), i
+        y_sum, total = ocpu.layernorm(x, gamma, beta, 1e-5, residual=res)
+        assert total.tobytes() == g[f"c{i}__sum"].tobytes(), i
+        assert y_sum.tobytes() == g[f"c{i}__y_sum"].tobytes(), i
+        q, s = ocpu.quantize_tensor(y)
+        assert s == float(g[f"c{i}__scale"]), i
+        np.testing.assert_array_equal(q, g[f"c{i}__q"], err_msg=str(i))
+
+
 def test_int8_gemm_and_epilogue_small():
     rs = np.random.RandomState(1)
     a = rs.randint(-127, 128, (33, 80)).astype(np.int8)

@@ -36,8 +36,8 @@ def test_interop_with_reference(tmp_path):
     """A checkpoint written here loads in the reference and vice versa."""
     from kansaiml_b200 import serialize
     ref = refpkg.import_reference_kansai()
-    import kansai.serialize as rser
-    import kansai.nn as rnn
+    import kansai_reference.serialize as rser
+    import kansai_reference.nn as rnn
     ours = _mlp(3)
     p1 = str(tmp_path / "ours.kan")
     serialize.save(ours, p1)
