@@ -1,30 +1,40 @@
 """Benchmark of Kansai's int8 quantized-linear hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
 
-Workload ("config 2"): one per-channel int8
-quantized Linear, fp32 weight [4096, 4096] ~ N(0, 0.02) quantized once per
-output channel, fp32 activations [2048, 4096] ~ N(0, 1).  One step = one
-forward of that layer over one batch of 2048 tokens: per-tensor activation
-absmax + quantize (one HBM-bound cooperative launch), then the tcgen05 int8
-GEMM with the per-row x per-channel rescale fused into its epilogue, fp32
-output.  Weight
-quantization is the layer's one-time construction (QLinear.__init__), as in
-the reference (quantize.py:139-141), and is not in the step.
+Default workload ("config 5", the north star's
+sharded matmul): a stack of 4 int8 Linear layers [16384 -> 16384], weights
+~ N(0, 0.01) quantized per output channel and column-sharded over the N ranks
+(Shard(1) of the reference's [in, out] weight), activations fp32
+[8192, 16384] ~ N(0, 1) row-sharded over the ranks and quantized per tensor.
+One step = one forward of the stack over the 8192-token batch: each rank
+quantizes its input rows (global absmax by an NCCL MAX all-reduce), the int8
+codes are all-gathered in row chunks while the first layer's GEMM consumes the
+chunks already present, and between layers the GEMM epilogues' absmax is
+all-reduced, each rank quantizes its output columns and the codes are
+all-gathered (again chunk by chunk, overlapped with the next GEMM).  Total
+work is fixed as N grows ("strong" scaling); N = 1 runs the same stack on one
+GPU with no collective.  Inputs are larger than L2 (weights 1 GiB of int8
+codes, input 512 MiB fp32).
 
-Inputs exceed L2: 4 rotating sets of (X fp32, weight codes, Y fp32) = 336 MB,
-so every step reads cold data.  Timing: W warm-up steps, then K steps (CUDA
-graphs of 8 steps replayed back to back) between barrier + synchronize on
-both sides, CUDA events on the launching stream, max over ranks.  N > 1 (torchrun): activations row-sharded, weights replicated:
-every rank runs its own 2048-token batch, no collective on the data path
-("weak" scaling).
+At N = 1 the line also carries, under "kernels", config 2 (one per-channel
+Linear [4096 -> 4096] over 2048 tokens: activation quantize + int8 GEMM) and
+each HBM-bound kernel of the path against the measured HBM peak.
 
---impl reference: the reference's own CPU implementation of this layer,
-qlinear (quantize.py:115-122) = dequantize the weight in Python, then the
-reference's C++ Tensor::matmul + add (oracle/_ref, compiled from the
-reference's sources), on a bounded row sample, rows spread over all host
-threads as the reference's Shard(0) DeviceMesh dispatch does
-(distributed.py:73-102).  Under torchrun only rank 0 runs it.
+Timing: W warm-up steps, then K steps between barrier + synchronize on both
+sides, CUDA events on the launching stream, max over ranks.
+
+--impl reference: the reference's own CPU implementation of the same
+workload: its only quantized Linear, qlinear (quantize.py:115-122:
+dequantize the int8 weight in Python every call, then the compiled
+reference core's Tensor::matmul + add, oracle/_ref), four layers.  A full
+step would take tens of minutes, so each step times a bounded sample -- the
+Python dequantize of 1/64 of one layer's weight and the matmul of one row per
+host thread against the full weight -- and scales it to the workload (4
+layers x 64 slices, 8192 / threads rows).  Under torchrun only rank 0 runs it.
+
+Other workloads (--workload): linear (config 2 as its own line), transformer
+(config 3), sweep (config 4), mlp (config 1).
 """
 import argparse
 import json
@@ -39,28 +49,37 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+METRIC = "int8 GEMM TOPS & quantized-linear tokens/s vs int8 roofline at 1/2/4/8 B200"
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+
+STACK_M, STACK_D, STACK_L = 8192, 16384, 4
+STACK_WORKLOAD = ("config5: 4 x int8 Linear [16384 -> 16384], weights per-channel int8 column-sharded over the "
+                  "ranks, activations [8192, 16384] row-sharded, quantized per tensor, int8 all-gather between "
+                  "layers, fp32 out")
 M_TOK, K_IN, N_OUT = 2048, 4096, 4096
 NSETS = 4
-METRIC = "int8 GEMM TOPS & quantized-linear tokens/s vs int8 roofline at 1/2/4/8 B200"
-WORKLOAD = ("config2: per-channel int8 quantized Linear [4096 -> 4096], 2048 tokens/step/GPU, "
-            "per-tensor activation quant, fused rescale, fp32 out")
-FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+LINEAR_WORKLOAD = ("config2: per-channel int8 quantized Linear [4096 -> 4096], 2048 tokens/step/GPU, "
+                   "per-tensor activation quant, fused rescale, fp32 out")
+WORKLOAD = STACK_WORKLOAD
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel entries (N = 1)")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="replay the stack's forward from a CUDA graph (auto: when capture succeeds)")
     ap.add_argument("--exchange", choices=["peer", "collective", "fused"], default=None,
-                    help="stack workload, N > 1: plain NCCL all-gather (collective, default) or the copy-engine "
-                         "all-gather overlapped with the gated GEMM (peer)")
-    ap.add_argument("--workload", choices=["linear", "stack", "transformer", "sweep", "mlp"], default="linear",
-                    help="linear: config 2 (default); stack: config 5, column-sharded 4-layer stack; "
-                         "transformer: config 3 decoder; sweep: config 4 square GEMMs; mlp: config 1")
+                    help="stack: pipelined NCCL all-gathers (collective, default), copy-engine pulls feeding the "
+                         "gated GEMM (peer) or the all-gather inside the GEMM launch (fused)")
+    ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp"], default="stack",
+                    help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
+                         "mlp: config 1")
     return ap.parse_args()
 
 
@@ -142,18 +161,12 @@ class ClockSampler:
 
 # --------------------------------------------------------- reference (CPU)
 
-def reference_sample_step(core, q_list, scale, shape, x_parts, bias_t, threads):
-    """One qlinear call of the reference (quantize.py:115-122) on the row sample:
-    dequantize in Python (quantize.py:76-77), then the compiled reference core's
-    Tensor::matmul + add per row part on its own thread (GIL released)."""
-    flat = [v * scale for v in q_list]
-    w = core.from_flat(flat, shape)
-    out = [None] * len(x_parts)
+def _parallel(fns):
+    out = [None] * len(fns)
 
     def work(i):
-        out[i] = x_parts[i].matmul(w).add(bias_t)
-
-    ts = [threading.Thread(target=work, args=(i,)) for i in range(len(x_parts))]
+        out[i] = fns[i]()
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(len(fns))]
     for t in ts:
         t.start()
     for t in ts:
@@ -161,105 +174,244 @@ def reference_sample_step(core, q_list, scale, shape, x_parts, bias_t, threads):
     return out
 
 
-def reference_setup(rows_per_thread=8):
-    from oracle import cpu as ocpu
-    from oracle.refpkg import load_reference_core
-    core = load_reference_core()
-    threads = os.cpu_count() or 1
-    rs = np.random.RandomState(7)
-    w = (rs.standard_normal((K_IN, N_OUT)) * 0.02).astype(np.float32)
-    q, scale = ocpu.quantize_tensor(w)           # the reference's per-tensor scheme
-    rows = rows_per_thread * threads
-    x = rs.standard_normal((rows, K_IN)).astype(np.float32)
-    parts = [core.from_flat(p.ravel().tolist(), [p.shape[0], K_IN]) for p in np.array_split(x, threads)]
-    bias = core.from_flat([0.0] * N_OUT, [N_OUT])
-    return core, q.ravel().tolist(), float(scale), [K_IN, N_OUT], parts, bias, threads, rows
+class ReferenceStackSample:
+    """Config 5 on the reference's CPU path, sampled: per layer the reference
+    runs qlinear = Python dequantize of the whole weight (quantize.py:76-77,
+    from_flat) + Tensor::matmul + add (compiled reference core).  One sample
+    step times the dequantize of 1/64 of a layer's codes and the matmul of one
+    row per host thread against the full [16384, 16384] weight (made inside
+    the reference core by its own randn; the naive loop's time does not depend
+    on the values), and scales both to the full step."""
+
+    SLICES = 64
+
+    def __init__(self):
+        from oracle.refpkg import load_reference_core
+        self.core = core = load_reference_core()
+        self.threads = os.cpu_count() or 1
+        D = STACK_D
+        self.w = core.randn([D, D], 0.01, False, 5)
+        rs = np.random.RandomState(9)
+        self.q_slice = rs.randint(-127, 128, D * D // self.SLICES).tolist()
+        self.scale = 4 * 0.01 / 127.0
+        self.parts = [core.randn([1, D], 1.0, False, 100 + i) for i in range(self.threads)]
+        self.bias = core.zeros([D])
+
+    def step(self):
+        """Seconds of one full config-5 step, extrapolated from one sample."""
+        t0 = time.perf_counter()
+        flat = [v * self.scale for v in self.q_slice]                 # quantize.py:76
+        self.core.from_flat(flat, [STACK_D // self.SLICES, STACK_D])  # quantize.py:77
+        t1 = time.perf_counter()
+        _parallel([lambda x=x: x.matmul(self.w).add(self.bias) for x in self.parts])
+        t2 = time.perf_counter()
+        per_layer = (t1 - t0) * self.SLICES + (t2 - t1) * (STACK_M / self.threads)
+        return STACK_L * per_layer, t2 - t0
+
+    def describe(self):
+        return (f"reference qlinear chain, 4 layers [16384 -> 16384] x 8192 rows, sampled per step: Python "
+                f"dequantize + from_flat of 1/{self.SLICES} of a layer's weight (x {self.SLICES}) and Tensor::matmul"
+                f" + add of 1 row on each of {self.threads} threads against the full weight "
+                f"(x {STACK_M // self.threads}), times 4 layers")
 
 
-def time_reference(steps, warmup, budget_s=None):
-    """Times `steps` reference qlinear calls (after `warmup`); with a budget,
-    runs as many of the requested steps as fit in it.  Returns
-    (tokens/s, seconds per step, threads, rows per step, steps timed)."""
-    core, ql, scale, shape, parts, bias, threads, rows = reference_setup()
-    t_w = time.perf_counter()
+class ReferenceLinear:
+    """Config 2 on the reference's CPU path, the full 2048-row batch per call:
+    qlinear (quantize.py:115-122) = one Python dequantize of the per-tensor
+    int8 weight (16.8 M codes) + from_flat, then Tensor::matmul + add, the
+    rows split over the host threads as the reference's Shard(0) DeviceMesh
+    dispatch does (distributed.py:73-102)."""
+
+    def __init__(self):
+        from oracle import cpu as ocpu
+        from oracle.refpkg import load_reference_core
+        self.core = core = load_reference_core()
+        self.threads = os.cpu_count() or 1
+        rs = np.random.RandomState(7)
+        w = (rs.standard_normal((K_IN, N_OUT)) * 0.02).astype(np.float32)
+        q, self.scale = ocpu.quantize_tensor(w)            # the reference's per-tensor scheme
+        self.q = q.ravel().tolist()
+        x = rs.standard_normal((M_TOK, K_IN)).astype(np.float32)
+        self.parts = [core.from_flat(p.ravel().tolist(), [p.shape[0], K_IN]) for p in np.array_split(x, self.threads)]
+        self.bias = core.from_flat([0.0] * N_OUT, [N_OUT])
+
+    def step(self):
+        t0 = time.perf_counter()
+        w = self.core.from_flat([v * self.scale for v in self.q], [K_IN, N_OUT])
+        _parallel([lambda x=x: x.matmul(w).add(self.bias) for x in self.parts])
+        dt = time.perf_counter() - t0
+        return dt, dt
+
+    def describe(self):
+        return (f"reference qlinear on the full 2048-row config-2 batch per call: one Python dequantize of the "
+                f"4096 x 4096 weight (quantize.py:121) + Tensor::matmul + add, rows split over {self.threads} threads")
+
+
+def time_reference(kind, steps, warmup, budget_s=None):
+    """(tokens/s, seconds per step, threads, sample text, steps timed, wall
+    seconds spent) of the reference arm for the workload `kind`."""
+    ref = ReferenceStackSample() if kind == "stack" else ReferenceLinear()
+    tokens = STACK_M if kind == "stack" else M_TOK
+    spent = 0.0
     for _ in range(max(warmup, 1)):
-        reference_sample_step(core, ql, scale, shape, parts, bias, threads)
-    est = (time.perf_counter() - t_w) / max(warmup, 1)
+        spent += ref.step()[1]
+    per = spent / max(warmup, 1)
     if budget_s is not None:
-        steps = max(1, min(steps, int(budget_s / max(est, 1e-6))))
-    t0 = time.perf_counter()
+        steps = max(1, min(steps, int(budget_s / max(per, 1e-6))))
+    est = []
     for _ in range(steps):
-        reference_sample_step(core, ql, scale, shape, parts, bias, threads)
-    dt = (time.perf_counter() - t0) / steps
-    return rows / dt, dt, threads, rows, steps
+        full, wall = ref.step()
+        est.append(full)
+        spent += wall
+    dt = sum(est) / len(est)
+    return tokens / dt, dt, ref.threads, ref.describe(), steps, spent
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    kind = "stack" if args.workload == "stack" else "linear"
     try:
-        value, dt, threads, rows, timed = time_reference(args.steps, min(args.warmup, 1), budget_s=120.0)
+        value, dt, threads, sample, timed, _ = time_reference(kind, args.steps, min(args.warmup, 1), budget_s=120.0)
     except Exception as e:  # the compiled reference core is missing
         print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path could not run: {e}"}))
         return
-    sample = (f"reference qlinear on {rows} of 2048 rows of config 2 (weight dequantized in Python every call, "
-              f"quantize.py:121, then Tensor::matmul + add split over {threads} threads)")
+    workload = STACK_WORKLOAD if kind == "stack" else LINEAR_WORKLOAD
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": timed, "steps_requested": args.steps, "warmup": min(args.warmup, 1), "ms_per_step": dt * 1e3,
-            "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": M_TOK, "parallelism": "host threads",
-                       "reference_path": "the reference's only qlinear: per-tensor int8 weight dequantized to fp32 "
+            "higher_is_better": True, "scaling": "strong" if kind == "stack" else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": STACK_M if kind == "stack" else M_TOK,
+                       "parallelism": "host threads",
+                       "reference_path": "the reference's only quantized Linear: int8 weight dequantized to fp32 "
                                          "every call (quantize.py:115-122), fp32 Tensor::matmul + add"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
-def cpu_baseline():
+def port_stack_sample():
+    """The C restatement (oracle/kz_oracle.c) of the W8A8 stack on all host
+    threads, sampled: the per-tensor quantize of 64 activation rows, the
+    int8 GEMM of those rows against one layer's codes and the epilogue; the
+    full step scales the GEMM and epilogue by 8192 / 64 rows and 4 layers and
+    adds the quantize of the full activation tensor per layer."""
+    from oracle import cpu as ocpu
+    rs = np.random.RandomState(11)
+    rows = 64
+    x = rs.standard_normal((rows, STACK_D)).astype(np.float32)
+    wq = rs.randint(-127, 128, (STACK_D, STACK_D), dtype=np.int8)
+    ws = np.full(STACK_D, 1e-4)
+    t0 = time.perf_counter()
+    xq, xs = ocpu.quantize_tensor(x)
+    t1 = time.perf_counter()
+    acc = ocpu.gemm_i8(xq, wq)
+    ocpu.epilogue(acc, xs, ws)
+    t2 = time.perf_counter()
+    per_layer = (t1 - t0) * (STACK_M / rows) + (t2 - t1) * (STACK_M / rows)
+    step = STACK_L * per_layer
+    return {"value": STACK_M / step, "unit": "tokens/s", "cores": ocpu.default_threads(), "kind": "port",
+            "sample": f"oracle/kz_oracle.c W8A8 layer (per-tensor quantize, int8 GEMM, epilogue) on {rows} of 8192 "
+                      f"rows, all host threads, scaled to 8192 rows x 4 layers",
+            "ms_per_step": step * 1e3}
+
+
+def cpu_baseline(kind):
     try:
-        value, dt, threads, rows, _ = time_reference(steps=3, warmup=1)
-        return {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                "sample": f"reference qlinear (quantize.py:115-122; dequantize in Python each call, compiled "
-                          f"reference Tensor::matmul + add) on {rows} rows of config 2, 3 timed calls, "
-                          f"{threads} threads"}
+        value, dt, threads, sample, timed, spent = time_reference(kind, steps=3, warmup=1)
+        out = {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+               "sample": f"{sample}; {timed} timed samples", "ms_per_step": dt * 1e3}
     except Exception as e:
-        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+        out = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    if kind == "stack":
+        try:
+            out["port"] = port_stack_sample()
+        except Exception as e:
+            out["port"] = {"value": None, "sample": f"unavailable: {e}"}
+    return out
 
 
-# ---------------------------------------------------------------- our path
+# ---------------------------------------------------------------- helpers
 
-def main():
-    args = parse()
-    if args.impl == "reference":
-        run_reference(args)
-        return
+def _events(dev):
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _graph_of(fn, reps, dev):
+    """A CUDA graph of `reps` calls of fn (warmed up eagerly first)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(reps):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def _time_graph(g, reps_per_graph, steps, warmup, local_rank, dev):
+    """Replays g until `steps` calls ran; returns (ms per call, calls, clocks)."""
+    import torch
+    for _ in range(max(1, -(-warmup // reps_per_graph))):
+        g.replay()
+    torch.cuda.synchronize()
+    n = max(1, -(-steps // reps_per_graph))
+    stream = torch.cuda.current_stream(dev)
+    start, end = _events(dev)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for _ in range(n):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    return start.elapsed_time(end) / (n * reps_per_graph), n * reps_per_graph, clk.summary()
+
+
+def _kernel_us(fn, dev, reps=16, replays=8):
+    """Average device time (us) of one call of fn: a CUDA graph of `reps`
+    calls replayed `replays` times back to back, CUDA events around the
+    replays only."""
+    import torch
+    g = _graph_of(fn, reps, dev)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = _events(dev)
+    stream = torch.cuda.current_stream(dev)
+    a.record(stream)
+    for _ in range(replays):
+        g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / (reps * replays) * 1e3
+
+
+def _sh(dev):
+    import torch
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ok(st):
+    from kansaiml_b200 import _lib
+    if st:
+        raise RuntimeError(_lib.last_error())
+
+
+# ------------------------------------------------------- config 2 (linear)
+
+def measure_linear(args, rank, world, local_rank, dev, steps, with_e2e):
+    """Config 2: one per-channel int8 Linear [4096 -> 4096] over 2048 tokens
+    per step and per rank.  Four rotating (X, W, Y) sets (336 MB > L2); steps
+    run from CUDA graphs of 8 steps (activation quantize + GEMM, PDL between
+    them).  Returns the measurements as a dict."""
     import torch
     import torch.distributed as dist
-
-    rank, world, local_rank = dist_env()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        import datetime
-        # The communicator's set-up prints a version banner on stdout (file
-        # descriptor 1); stdout carries only rank 0's JSON line, so fd 1
-        # points at stderr while the group and its communicator come up.
-        sys.stdout.flush()
-        saved_fd = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-            dist.barrier()
-        finally:
-            sys.stdout.flush()
-            os.dup2(saved_fd, 1)
-            os.close(saved_fd)
-    if args.workload != "linear":
-        {"stack": run_stack, "transformer": run_transformer, "sweep": run_sweep, "mlp": run_mlp}[args.workload](
-            args, rank, world, local_rank, dev)
-        return
 
     import kansaiml_b200 as kz
     from kansaiml_b200 import _lib
@@ -267,9 +419,8 @@ def main():
 
     lib = _lib.load()
     rs = np.random.RandomState(1000 + rank)
-    # one-time layer construction: NSETS independent weights, quantized per channel
     layers = []
-    for i in range(NSETS):
+    for _ in range(NSETS):
         w = torch.from_numpy((rs.standard_normal((K_IN, N_OUT)) * 0.02).astype(np.float32)).to(dev)
 
         class _Lin:
@@ -291,38 +442,21 @@ def main():
     XQ, S64, S32, PP = xq.data_ptr(), s64.data_ptr(), s32.data_ptr(), partials.data_ptr()
 
     def quantize_only(i):
-        """The activation absmax + quantize of set i % NSETS (one cooperative launch)."""
-        sh = torch.cuda.current_stream(dev).cuda_stream
-        if lib.kz_quantize_tensor_f32(X[i % NSETS], n_el, XQ, S64, S32, PP, sh):
-            raise RuntimeError(_lib.last_error())
+        _ok(lib.kz_quantize_tensor_f32(X[i % NSETS], n_el, XQ, S64, S32, PP, _sh(dev)))
 
     def gemm_only(i):
-        """The int8 GEMM with fused rescale of set i % NSETS."""
         j = i % NSETS
-        sh = torch.cuda.current_stream(dev).cuda_stream
-        if lib.kz_gemm_i8(XQ, B[j][0], M_TOK, N_OUT, K_IN, K_IN, S32, 0, B[j][1], 1, None, 0, Y[j], None, N_OUT,
-                          None, sh):
-            raise RuntimeError(_lib.last_error())
+        _ok(lib.kz_gemm_i8(XQ, B[j][0], M_TOK, N_OUT, K_IN, K_IN, S32, 0, B[j][1], 1, None, 0, Y[j], None, N_OUT,
+                           None, _sh(dev)))
 
     def step(i):
-        """One forward of the layer on rotating set i % NSETS: activation absmax +
-        quantize (one cooperative launch), int8 GEMM with fused rescale."""
         quantize_only(i)
         gemm_only(i)
 
-    # first step eagerly (sets up per-device state), then check the device status
     step(0)
     torch.cuda.synchronize()
     if kq.device_status() != 0:
         raise RuntimeError("device status set after the first step")
-
-    # Timed steps run from CUDA graphs of S consecutive steps (2 kernel nodes
-    # each, no event nodes), replayed back to back, as a model captures its
-    # layers.  A second pass times each kernel alone: graphs of S launches of
-    # just that kernel over the same rotating sets, replayed back to back with
-    # CUDA events only around the replays (event nodes between the two kernels
-    # of a step would break their programmatic dependent launch and add the
-    # gaps to both), for the per-kernel and roofline figures.
     S = 8
     cap_stream = torch.cuda.Stream(dev)
 
@@ -333,14 +467,12 @@ def main():
                 fn(i)
         return gr
 
-    K = args.steps
+    K = steps
     chunk_graph = capture(range(S))
     tail_graph = capture(range(K % S)) if K % S else None
     quant_graph = capture(range(S), quantize_only)
     gemm_graph = capture(range(S), gemm_only)
     torch.cuda.synchronize()
-
-    # warm-up: at least W steps, through the same graphs the timed region replays
     for _ in range(max(1, -(-args.warmup // S))):
         chunk_graph.replay()
     if tail_graph is not None:
@@ -349,7 +481,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start, end = _events(dev)
     with ClockSampler(local_rank) as clk:
         start.record(stream)
         for _ in range(K // S):
@@ -361,14 +493,13 @@ def main():
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
-    # per-kernel device times: as many launches of each kernel alone as the timed region made
     reps = max(1, K // S)
 
     def kernel_ms(gr):
         for _ in range(2):
             gr.replay()
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a, b = _events(dev)
         a.record(stream)
         for _ in range(reps):
             gr.replay()
@@ -377,33 +508,71 @@ def main():
         return a.elapsed_time(b) / (reps * S)
     quant_avg = kernel_ms(quant_graph)
     gemm_avg = kernel_ms(gemm_graph)
+    del chunk_graph, tail_graph, quant_graph, gemm_graph
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / K
-    tokens = M_TOK * world
-    value = tokens / (ms_per_step / 1e3)
+    hbm_gbs, bf16, _, peak_src = peaks()
+    int8_peak = 2.0 * bf16
     ops = 2.0 * M_TOK * N_OUT * K_IN
-    hbm_gbs, bf16, bf16_sus, peak_src = peaks()
-    int8_peak = 2.0 * bf16   # B200 int8 dense rate is 2x its bf16 dense rate
     tops = ops / (gemm_avg / 1e3) / 1e12
-    # algorithmic bytes: absmax pass 4 B/element + quantize pass 4 + 1 B/element,
-    # counted per pass although the single launch reads x from HBM once
-    quant_bytes = 9.0 * n_el
-
-    # ------------------------------------------------------------ e2e
-    # Through the public API with host buffers: every step copies its pinned
-    # host X to the device, runs QLinear, and copies its fp32 Y back to pinned
-    # host memory.  Copies run on their own streams over NB buffers, so step
-    # i's upload, earlier steps' forwards and downloads overlap (PCIe carries
-    # both directions at once); every step still moves its own bytes.
+    out = {"workload": LINEAR_WORKLOAD, "tokens_per_s": M_TOK * world / (ms_per_step / 1e3),
+           "ms_per_step": ms_per_step, "steps": K, "clocks": clk.summary(),
+           "launch": f"CUDA graphs of {S} steps (2 libkz kernels per step) replayed back to back",
+           "l2": f"inputs larger than L2: {NSETS} rotating (X, W, Y) sets, "
+                 f"{NSETS * (M_TOK * K_IN * 4 + K_IN * N_OUT + M_TOK * N_OUT * 4) / 1e6:.0f} MB",
+           "gemm": {"kernel": "gemm_i8_kernel", "bound": "tensor", "avg_us": gemm_avg * 1e3, "achieved": tops,
+                    "peak": int8_peak, "unit": "TOP/s", "frac": tops / int8_peak,
+                    "traffic": profile_traffic("gemm_i8_config2"),
+                    "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
+                    "algorithmic": f"2*M*N*K = {ops:.3e} op per launch",
+                    "timing": f"CUDA events around {reps} replays of a graph of {S} launches of this kernel alone"},
+           "quantize_activations": _hbm_entry("quantize_resident_kernel", quant_avg * 1e3, 9.0 * n_el, hbm_gbs,
+                                              "9 B/element algorithmic (absmax 4 + quantize 4 + 1, per pass)",
+                                              dram_bytes=5.0 * n_el)}
+    if not with_e2e:
+        return out
+    # e2e through the public API with host buffers (pinned), three buffers in flight
     NB = 3
     x_host = [torch.from_numpy(rs.standard_normal((M_TOK, K_IN)).astype(np.float32)).pin_memory() for _ in range(NB)]
     y_host = [torch.empty((M_TOK, N_OUT), dtype=torch.float32).pin_memory() for _ in range(NB)]
     x_dev = [torch.empty((M_TOK, K_IN), dtype=torch.float32, device=dev) for _ in range(NB)]
-    y_dev = [None] * NB
     layer = layers[0]
+
+    def forward(xd):
+        return layer(kz.Tensor(xd)).data
+
+    e2e_ms = _e2e_loop(forward, x_host, y_host, x_dev, args.e2e_steps, world, dev)
+    out["e2e"] = {"value": M_TOK * world / (e2e_ms / args.e2e_steps / 1e3), "unit": "tokens/s",
+                  "h2d_bytes_per_step": M_TOK * K_IN * 4, "d2h_bytes_per_step": M_TOK * N_OUT * 4}
+    return out
+
+
+def _hbm_entry(kernel, avg_us, alg_bytes, hbm_gbs, algorithmic, dram_bytes=None):
+    gbs = alg_bytes / (avg_us / 1e6) / 1e9
+    e = {"kernel": kernel, "bound": "hbm", "avg_us": avg_us, "achieved_gbs": gbs, "peak_gbs": hbm_gbs,
+         "frac": gbs / hbm_gbs, "algorithmic": algorithmic}
+    if dram_bytes is not None:
+        d = dram_bytes / (avg_us / 1e6) / 1e9
+        e["dram_bytes_per_launch"] = dram_bytes
+        e["achieved_gbs_dram"] = d
+        e["frac_dram"] = d / hbm_gbs
+    return e
+
+
+def _e2e_loop(forward, x_host, y_host, x_dev, steps, world, dev):
+    """Every step copies its pinned host input to the device (copy stream),
+    runs `forward` on the compute stream and copies the result back to pinned
+    host memory (another copy stream); NB buffers in flight, so uploads,
+    forwards and downloads of neighbouring steps overlap while every step
+    still moves its own bytes.  Returns device ms for `steps` steps, max over
+    ranks."""
+    import torch
+    import torch.distributed as dist
+    NB = len(x_host)
+    stream = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(NB)]
     ev_fwd = [torch.cuda.Event() for _ in range(NB)]
@@ -418,90 +587,150 @@ def main():
             x_dev[b].copy_(x_host[b], non_blocking=True)
             ev_in[b].record(s_in)
         stream.wait_event(ev_in[b])
-        stream.wait_event(ev_out[b])              # y_dev[b] of NB steps ago has been read back
-        y_dev[b] = layer(kz.Tensor(x_dev[b])).data
+        stream.wait_event(ev_out[b])              # y of NB steps ago has been read back
+        y = forward(x_dev[b])
         ev_fwd[b].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_fwd[b])
-            y_host[b].copy_(y_dev[b], non_blocking=True)
-            y_dev[b].record_stream(s_out)
+            y_host[b].copy_(y, non_blocking=True)
+            y.record_stream(s_out)
             ev_out[b].record(s_out)
 
-    for i in range(3):
+    for i in range(NB):
         e2e_step(i)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = _events(dev)
     e0.record(stream)
-    for i in range(args.e2e_steps):
+    for i in range(steps):
         e2e_step(i)
     stream.wait_stream(s_out)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    ms = e0.elapsed_time(e1)
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = tokens / (e2e_ms / args.e2e_steps / 1e3)
+        ms = float(t.item())
+    return ms
 
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline()
-    traffic = profile_traffic("gemm_i8_config2")
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD,
-                   "launch": f"CUDA graphs of {S} steps (2 libkz kernels per step) replayed back to back",
-                   "global_batch": tokens, "seq_len": None, "parallelism": f"dp{world} (row-sharded activations)",
-                   "l2": f"inputs larger than L2: {NSETS} rotating (X, W, Y) sets, "
-                         f"{NSETS * (M_TOK * K_IN * 4 + K_IN * N_OUT + M_TOK * N_OUT * 4) / 1e6:.0f} MB"},
-        "tops": ops * world / (ms_per_step / 1e3) / 1e12,
-        "gpu_launches": 2 * K,
-        "roofline": {"kernel": "gemm_i8_kernel", "bound": "tensor", "achieved": tops, "peak": int8_peak,
-                     "unit": "TOP/s", "frac": tops / int8_peak, "traffic": traffic,
-                     "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
-                     "avg_launch_us": gemm_avg * 1e3,
-                     "timing": f"CUDA events around {reps} back-to-back replays of a graph of {S} launches of "
-                               "this kernel alone over the same rotating sets, right after the timed region",
-                     "algorithmic": f"2*M*N*K = {ops:.3e} op per launch"},
-        "kernels": {"quantize_activations": {"avg_us": quant_avg * 1e3, "bound": "hbm",
-                                             "achieved_gbs": quant_bytes / (quant_avg / 1e3) / 1e9,
-                                             "peak_gbs": hbm_gbs, "frac": quant_bytes / (quant_avg / 1e3) / 1e9 / hbm_gbs,
-                                             "algorithmic": "9 B/element (absmax 4 + quantize 4+1, per pass; the launch reads x from HBM once, "
-                                                             "5 B/element of DRAM traffic)"}},
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": M_TOK * K_IN * 4,
-                "d2h_bytes_per_step": M_TOK * N_OUT * 4},
-        "cpu_baseline": cpu,
-        "clocks": clk.summary(),
-    }
-    print(json.dumps(line))
+
+# ----------------------------------------------- per-kernel HBM rooflines
+
+def measure_kernels(args, rank, world, local_rank, dev):
+    """N = 1: config 2 (quantize + GEMM step), the int8 GEMM at 8192^3, the
+    reference-semantics W8A32 qlinear at config 2's shape, and each HBM-bound
+    kernel of the path on rotating inputs larger than L2."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    hbm_gbs, bf16, _, peak_src = peaks()
+    int8_peak = 2.0 * bf16
+    out = {}
+    out["config2_linear"] = measure_linear(args, rank, world, local_rank, dev, steps=400, with_e2e=False)
+    torch.cuda.empty_cache()
+    i = [0]
+
+    def nxt(n):
+        i[0] += 1
+        return i[0] % n
+
+    # int8 GEMM 8192^3, per-row x per-column scale epilogue (config 4's headline size)
+    n = 8192
+    g = torch.Generator(device=dev)
+    g.manual_seed(8192)
+    sets = [(torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g),
+             torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g),
+             torch.rand(n, device=dev, generator=g) * 9e-3 + 1e-3, torch.rand(n, device=dev, generator=g) * 9e-3 + 1e-3,
+             torch.empty((n, n), dtype=torch.float32, device=dev)) for _ in range(2)]
+
+    def gemm8k():
+        a, b, rs_, cs_, y = sets[nxt(2)]
+        _ok(lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, rs_.data_ptr(), 1, cs_.data_ptr(), 1, None, 0,
+                           y.data_ptr(), None, n, None, _sh(dev)))
+    us = _kernel_us(gemm8k, dev, reps=4, replays=6)
+    tops = 2.0 * n ** 3 / (us / 1e6) / 1e12
+    out["gemm_8192_cubed"] = {"kernel": "gemm_i8_kernel", "bound": "tensor", "avg_us": us, "achieved": tops,
+                              "peak": int8_peak, "unit": "TOP/s", "frac": tops / int8_peak,
+                              "algorithmic": "2*8192^3 op per launch, fp32 epilogue (per-row x per-column scales)"}
+    del sets
+    torch.cuda.empty_cache()
+    # W8A32 qlinear (the reference's own semantics) at config 2's shape
+    xw = [torch.randn((M_TOK, K_IN), device=dev) for _ in range(2)]
+    qw = torch.randint(-127, 128, (K_IN, N_OUT), dtype=torch.int8, device=dev)
+    yw = torch.empty((M_TOK, N_OUT), device=dev)
+
+    def w8a32():
+        _ok(lib.kz_qlinear_w8a32_f32(xw[nxt(2)].data_ptr(), M_TOK, K_IN, qw.data_ptr(), 0.02 / 127, None, N_OUT, 0,
+                                     yw.data_ptr(), _sh(dev)))
+    us = _kernel_us(w8a32, dev, reps=2, replays=3)
+    flops = 2.0 * M_TOK * N_OUT * K_IN
+    props = torch.cuda.get_device_properties(dev)
+    fp32_peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12
+    tf = flops / (us / 1e6) / 1e12
+    out["w8a32_qlinear_config2"] = {
+        "kernel": "qlinear_w8a32_kernel", "bound": "fp32 SIMT (k-ordered)", "avg_us": us, "achieved": tf,
+        "unit": "TFLOP/s", "peak": fp32_peak / 2, "frac": tf / (fp32_peak / 2),
+        "peak_source": f"{props.multi_processor_count} SMs x 128 fp32 lanes x 1.965 GHz = {fp32_peak:.1f} TFLOP/s "
+                       "of FMA; the reference's loop rounds each product and sum separately (no FMA), so 2 "
+                       "instructions per multiply-add: half that",
+        "algorithmic": f"2*M*N*K = {flops:.3e} flop per call, per-tensor int8 weight, fp32 activations"}
+    del xw, qw, yw
+    # dequantize, 8.4 M codes (config 2's activation size), 4 rotating sets
+    nd = M_TOK * K_IN
+    qs = [torch.randint(-127, 128, (nd,), dtype=torch.int8, device=dev) for _ in range(NSETS)]
+    ds = [torch.empty(nd, device=dev) for _ in range(NSETS)]
+
+    def deq():
+        j = nxt(NSETS)
+        _ok(lib.kz_dequantize_i8_f32(qs[j].data_ptr(), nd, 0.01, ds[j].data_ptr(), _sh(dev)))
+    out["dequantize"] = _hbm_entry("dequantize_kernel", _kernel_us(deq, dev), 5.0 * nd, hbm_gbs,
+                                   "5 B/element (1 B code in, 4 B fp32 out)", dram_bytes=5.0 * nd)
+    del qs, ds
+    # per-channel weight quantize, config 2's 4096 x 4096 weight (absmax_cols4 + quantize_cols4)
+    ws = [torch.randn((K_IN, N_OUT), device=dev) * 0.02 for _ in range(NSETS)]
+    qT = torch.empty((N_OUT, K_IN), dtype=torch.int8, device=dev)
+    s64 = torch.empty(N_OUT, dtype=torch.float64, device=dev)
+    s32 = torch.empty(N_OUT, device=dev)
+    wsb = torch.empty(lib.kz_quantize_cols_workspace_bytes(K_IN, N_OUT), dtype=torch.uint8, device=dev)
+
+    def qcols():
+        _ok(lib.kz_quantize_cols_f32(ws[nxt(NSETS)].data_ptr(), K_IN, N_OUT, qT.data_ptr(), s64.data_ptr(),
+                                     s32.data_ptr(), wsb.data_ptr(), wsb.numel(), _sh(dev)))
+    ne = K_IN * N_OUT
+    out["quantize_cols"] = _hbm_entry("absmax_cols4_kernel + quantize_cols4_kernel", _kernel_us(qcols, dev),
+                                      9.0 * ne, hbm_gbs,
+                                      "9 B/element for the pair (absmax 4, quantize 4 + 1); the quantize pass "
+                                      "may re-read the 67 MB weight from L2", dram_bytes=5.0 * ne)
+    del ws, qT, wsb
+    # LayerNorm -> absmax partials (config 3's 8192 x 256 activations)
+    Ml, Dl = 8192, 256
+    lx = [torch.randn((Ml, Dl), device=dev) for _ in range(16)]
+    ly = [torch.empty((Ml, Dl), device=dev) for _ in range(16)]
+    gm, bt = torch.ones(Dl, device=dev), torch.zeros(Dl, device=dev)
+    lp = torch.zeros(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+
+    def lnorm():
+        j = nxt(16)
+        _ok(lib.kz_layernorm_partials_f32(lx[j].data_ptr(), Ml, Dl, gm.data_ptr(), bt.data_ptr(), 1e-5,
+                                          ly[j].data_ptr(), lp.data_ptr(), _sh(dev)))
+    out["layernorm"] = _hbm_entry("layernorm_partials_kernel", _kernel_us(lnorm, dev), 8.0 * Ml * Dl, hbm_gbs,
+                                  "8 B/element (4 in, 4 out); 16 rotating 8 MB sets (128 MB, about L2)")
+    del lx, ly
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------- config 5: sharded stack
 
-STACK_M, STACK_D, STACK_L = 8192, 16384, 4
-
-
 def run_stack(args, rank, world, local_rank, dev):
-    """4 int8 Linear layers [16384 -> 16384], weights
-    ~ N(0, 0.01) quantized per output channel and column-sharded over the
-    ranks, activations fp32 [8192, 16384] ~ N(0, 1) quantized per tensor and
-    all-gathered (int8, NCCL over NVLink) between layers.  One step = one
-    forward of the stack over the 8192-token batch; total work fixed as N grows
-    ("strong" scaling).  Output: each rank's fp32 column shard."""
     import torch
     import torch.distributed as dist
 
+    from kansaiml_b200 import _lib
     from kansaiml_b200.distributed import DeviceMesh, ShardedQLinearStack
+    from kansaiml_b200.quantize import device_status
 
     mesh = DeviceMesh.spmd() if world > 1 else None
 
@@ -511,88 +740,211 @@ def run_stack(args, rank, world, local_rank, dev):
         return torch.randn((STACK_D, STACK_D), generator=g, device=dev) * 0.01
 
     stack = ShardedQLinearStack([weight] * STACK_L, mesh, exchange=args.exchange)
+    M = STACK_M
     g = torch.Generator(device=dev)
     g.manual_seed(77)
-    x = torch.randn((STACK_M, STACK_D), generator=g, device=dev)
-    torch.cuda.synchronize()
+    x_full = torch.randn((M, STACK_D), generator=g, device=dev)
+    pipelined = stack.exchange == "collective"
+    x_local = stack.local_input(x_full) if (pipelined and world > 1) else x_full
+    if pipelined:
+        del x_full
+    torch.cuda.empty_cache()
+    C = stack.chunks(M) if pipelined else 1
+    if pipelined and world > 1:
+        # leave SMs for the NCCL all-gather that overlaps each GEMM chunk
+        _ok(_lib.load().kz_set_sm_count_target(max(2, torch.cuda.get_device_properties(dev).multi_processor_count - 16)))
+
+    def fwd():
+        if pipelined:
+            return stack.forward_local(x_local, M)
+        return stack(x_local)
+
     for _ in range(max(args.warmup, 3)):
-        stack(x)
+        fwd()
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise RuntimeError("device status set during warm-up")
+    graph, graph_note = None, "eager launches"
+    if args.graph != "off" and pipelined:
+        try:
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, stream=st):
+                fwd()
+            torch.cuda.synchronize()
+            g_.replay()
+            torch.cuda.synchronize()
+            graph, graph_note = g_, "one CUDA graph per step (the whole forward, NCCL collectives included)"
+        except Exception as e:  # capture unsupported: eager launches
+            if args.graph == "on":
+                raise
+            graph_note = f"eager launches (graph capture failed: {type(e).__name__})"
+            torch.cuda.synchronize()
+    # the same decision on every rank
+    if world > 1:
+        flag = torch.tensor([1 if graph is not None else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0 and graph is not None:
+            graph, graph_note = None, "eager launches (graph capture failed on another rank)"
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            fwd()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
     K = args.steps
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start, end = _events(dev)
     with ClockSampler(local_rank) as clk:
         start.record(stream)
         for _ in range(K):
-            stack(x)
+            step()
         end.record(stream)
         torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     ms = start.elapsed_time(end)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    ms_per_step = ms / K
+    status = device_status()
+
+    # per-phase device times of one eager forward (events on the compute stream)
+    phases = None
+    if pipelined:
+        stack.timing = True
+        for _ in range(2):
+            fwd()
+            phases = stack.phase_times()
+        stack.timing = False
+        if world > 1:
+            keys = sorted(phases)
+            t = torch.tensor([phases[k] for k in keys], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            phases = {k: float(v) for k, v in zip(keys, t.tolist())}
+
+    # the dominant kernel alone: the forward's GEMM launches (same shapes) back to back
+    n_loc = STACK_D // world
+    mc = M // C
+    qt0 = stack.layers[0][0]
+    a_chunk = torch.randint(-127, 128, (mc, STACK_D), dtype=torch.int8, device=dev)
+    ys = [torch.empty((mc, n_loc), dtype=torch.float32, device=dev) for _ in range(2)]
+    a_s = torch.full((1,), 1e-3, device=dev)
+    lib = _lib.load()
+    j = [0]
+
+    def gemm_launch():
+        j[0] += 1
+        qt = stack.layers[j[0] % STACK_L][0]
+        _ok(lib.kz_gemm_i8(a_chunk.data_ptr(), qt.kmajor().data_ptr(), mc, n_loc, STACK_D, STACK_D, a_s.data_ptr(),
+                           0, qt.scale_f32.data_ptr(), 1, None, 0, ys[j[0] % 2].data_ptr(), None, n_loc, None,
+                           _sh(dev)))
+    gemm_us = _kernel_us(gemm_launch, dev, reps=4 * C, replays=4)
+    del a_chunk, ys, qt0
+    hbm_gbs, bf16, bf16_sus, peak_src = peaks()
+    int8_peak = 2.0 * bf16
+    gemm_ops = 2.0 * mc * n_loc * STACK_D
+    gemm_tops = gemm_ops / (gemm_us / 1e6) / 1e12
+    # ours per step: input absmax + quantize, C GEMMs per layer, C quantizes per layer boundary
+    launches_per_step = (2 + STACK_L * C + (STACK_L - 1) * C) if pipelined else (1 + 2 * STACK_L - 1)
+
+    # e2e: host input rows in, this rank's fp32 output columns out, through the stack's public forward
+    NB = 3
+    rows = stack.input_rows(M) if pipelined else [(0, M)]
+    m_loc = sum(b - a for a, b in rows)
+    rs = np.random.RandomState(2000 + rank)
+    x_host = [torch.from_numpy(rs.standard_normal((m_loc, STACK_D)).astype(np.float32)).pin_memory()
+              for _ in range(NB)]
+    y_host = [torch.empty((M, n_loc), dtype=torch.float32).pin_memory() for _ in range(NB)]
+    x_dev = [torch.empty((m_loc, STACK_D), dtype=torch.float32, device=dev) for _ in range(NB)]
+    del x_local
+    torch.cuda.empty_cache()
+
+    def forward_host_rows(xd):
+        return (stack.forward_local(xd, M) if pipelined else stack(xd)).data
+
+    e2e_ms = _e2e_loop(forward_host_rows, x_host, y_host, x_dev, args.e2e_steps, world, dev)
+    e2e = {"value": M / (e2e_ms / args.e2e_steps / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": m_loc * STACK_D * 4 * world, "d2h_bytes_per_step": M * n_loc * 4 * world,
+           "note": "bytes summed over ranks: each rank uploads its input rows and downloads its output columns"}
+    del x_host, y_host, x_dev
+    torch.cuda.empty_cache()
+
+    kernels = None
+    if world == 1 and not args.no_kernels:
+        kernels = measure_kernels(args, rank, world, local_rank, dev)
+    if world > 1:
+        del graph
         stack.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    ms_per_step = ms / K
-    ops = 2.0 * STACK_M * STACK_D * STACK_D * STACK_L
-    tops = ops / (ms_per_step / 1e3) / 1e12
-    hbm_gbs, bf16, _, peak_src = peaks()
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline("stack")
+    ops = 2.0 * M * STACK_D * STACK_D * STACK_L
     line = {
-        "metric": METRIC, "value": STACK_M / (ms_per_step / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "metric": METRIC, "value": M / (ms_per_step / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "config5: 4 x int8 Linear [16384 -> 16384] column-sharded, 8192 tokens, per-tensor "
-                               "activation quant + NCCL all-gather between layers",
-                   "global_batch": STACK_M, "seq_len": None, "parallelism": f"tp{world} (column-sharded weights)",
-                   "exchange": stack.exchange,
-                   "l2": "inputs larger than L2 (weights 1 GiB int8 in total, activations 512 MiB fp32)"},
-        "tops": tops,
-        "roofline": {"kernel": "whole stack", "bound": "tensor", "achieved": tops, "peak": 2.0 * bf16 * world,
-                     "unit": "TOP/s", "frac": tops / (2.0 * bf16 * world), "traffic": None,
-                     "peak_source": f"{world} x 2 x bf16_tflops ({bf16:.1f}, {peak_src})"},
-        "gpu_launches": (1 + 2 * STACK_L - 1) * K,
+        "config": {"workload": STACK_WORKLOAD, "global_batch": M, "seq_len": None,
+                   "parallelism": f"tp{world} (weights column-sharded, activations row-sharded)",
+                   "exchange": stack.exchange, "row_chunks": C, "launch": graph_note,
+                   "l2": "inputs larger than L2 (weights 1 GiB int8 codes in total, input 512 MiB fp32)"},
+        "tops": ops / (ms_per_step / 1e3) / 1e12,
+        "gpu_launches": launches_per_step * K,
+        "roofline": {"kernel": "gemm_i8_kernel", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+                     "unit": "TOP/s", "frac": gemm_tops / int8_peak,
+                     "traffic": profile_traffic(f"gemm_i8_config5_tp{world}"),
+                     "avg_launch_us": gemm_us,
+                     "shape": f"M={mc} N={n_loc} K={STACK_D} (one row chunk of one layer on one rank)",
+                     "algorithmic": f"2*M*N*K = {gemm_ops:.3e} op per launch",
+                     "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
+                     "timing": f"CUDA events around 4 replays of a graph of the step's {4 * C} GEMM launches "
+                               "(same shapes and weights) alone, right after the timed region"},
+        "phases_ms": phases,
+        "device_status": status,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
         "clocks": clk.summary(),
     }
+    if kernels is not None:
+        line["kernels"] = kernels
     print(json.dumps(line))
 
 
+# ----------------------------------------------------------- other lines
 
-def _graph_of(fn, reps, dev):
-    """A CUDA graph of `reps` calls of fn (warmed up eagerly first)."""
-    import torch
-    fn()
-    torch.cuda.synchronize()
-    st = torch.cuda.Stream(dev)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=st):
-        for _ in range(reps):
-            fn()
-    torch.cuda.synchronize()
-    return g
-
-
-def _time_graph(g, reps_per_graph, steps, warmup, local_rank, dev):
-    """Replays g until `steps` calls ran; returns (ms per call, clocks)."""
-    import torch
-    for _ in range(max(1, -(-warmup // reps_per_graph))):
-        g.replay()
-    torch.cuda.synchronize()
-    n = max(1, -(-steps // reps_per_graph))
-    stream = torch.cuda.current_stream(dev)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        start.record(stream)
-        for _ in range(n):
-            g.replay()
-        end.record(stream)
-        torch.cuda.synchronize()
-    return start.elapsed_time(end) / (n * reps_per_graph), n * reps_per_graph, clk.summary()
+def run_linear(args, rank, world, local_rank, dev):
+    """Config 2 as its own line: N > 1 runs it data-parallel (each rank its
+    own 2048-token batch, weights replicated, no collective: "weak")."""
+    import torch.distributed as dist
+    r = measure_linear(args, rank, world, local_rank, dev, steps=args.steps, with_e2e=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None if (world > 1 or args.no_cpu_baseline) else cpu_baseline("linear")
+    line = {"metric": METRIC, "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": r["steps"],
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": LINEAR_WORKLOAD, "launch": r["launch"], "global_batch": M_TOK * world,
+                       "seq_len": None, "parallelism": f"dp{world} (row-sharded activations)", "l2": r["l2"]},
+            "gpu_launches": 2 * r["steps"], "roofline": r["gemm"],
+            "kernels": {"quantize_activations": r["quantize_activations"]},
+            "e2e": r["e2e"], "cpu_baseline": cpu, "clocks": r["clocks"]}
+    print(json.dumps(line))
 
 
 def run_transformer(args, rank, world, local_rank, dev):
@@ -600,7 +952,6 @@ def run_transformer(args, rank, world, local_rank, dev):
     GELU, vocab 65, context 256, batch 32 = 8192 tokens), per-channel int8
     weights, per-tensor int8 activations, fp32 LayerNorm / attention / softmax.
     One step = one forward of the batch, captured in a CUDA graph."""
-    import torch
     from kansaiml_b200 import workloads
 
     model = workloads.Decoder(seed=3, device=dev)
@@ -654,16 +1005,14 @@ def run_sweep(args, rank, world, local_rank, dev):
         res = {"n": n, "sets": nsets}
         for form in ("fp32_epilogue", "int32"):
             def call():
-                sh = torch.cuda.current_stream(dev).cuda_stream
                 for a, b, rs, cs, y in sets:
                     if form == "int32":
                         st = lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, None, 0, None, 0, None, 0, None,
-                                            y.data_ptr(), n, None, sh)
+                                            y.data_ptr(), n, None, _sh(dev))
                     else:
                         st = lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, rs.data_ptr(), 1, cs.data_ptr(), 1,
-                                            None, 0, y.data_ptr(), None, n, None, sh)
-                    if st:
-                        raise RuntimeError(_lib.last_error())
+                                            None, 0, y.data_ptr(), None, n, None, _sh(dev))
+                    _ok(st)
             reps = max(1, 16 // nsets) if n <= 4096 else 1
             gr = _graph_of(call, reps, dev)
             steps = max(4, min(args.steps, int(2e13 / (2.0 * n ** 3))))
@@ -696,7 +1045,6 @@ def run_mlp(args, rank, world, local_rank, dev):
     weights and fp32 activations: the reference's own semantics
     (qlinear = x @ dequantize(W) + b), bit-identical outputs.  One step = one
     forward, captured in a CUDA graph."""
-    import torch
     import kansaiml_b200 as kz
     from kansaiml_b200 import nn
     from kansaiml_b200.quantize import QLinear
@@ -720,6 +1068,38 @@ def run_mlp(args, rank, world, local_rank, dev):
         "clocks": clocks,
     }
     print(json.dumps(line))
+
+
+# ------------------------------------------------------------------- main
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local_rank = dist_env()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        # The communicator's set-up prints a version banner on stdout (file
+        # descriptor 1); stdout carries only rank 0's JSON line, so fd 1
+        # points at stderr while the group and its communicator come up.
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
+    {"stack": run_stack, "linear": run_linear, "transformer": run_transformer, "sweep": run_sweep,
+     "mlp": run_mlp}[args.workload](args, rank, world, local_rank, dev)
 
 
 if __name__ == "__main__":

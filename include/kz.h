@@ -217,6 +217,13 @@ int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K
                const float* bias, int act, float* out_f32, int32_t* out_i32, int64_t ldo,
                uint32_t* absmax_partials, kz_stream_t stream);
 
+/* Caps the SMs that the int8 GEMMs launched on the current device afterwards
+ * use (0, the default: every SM), so that a kernel running at the same time on
+ * another stream -- an NCCL all-gather overlapped with the GEMM of the chunk
+ * before it -- finds SMs free instead of waiting behind a persistent grid.
+ * The same knob as cublasSetSmCountTarget.  No reference counterpart. */
+int kz_set_sm_count_target(int sms);
+
 /* kz_gemm_i8 with its A operand in the blocked layout [G][M][a_kblock]
  * (G = K / a_kblock <= 32) still being assembled while the kernel runs (no
  * reference counterpart; config 5's all-gather overlapped with the next

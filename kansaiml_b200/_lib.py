@@ -46,6 +46,7 @@ SIGNATURES = {
     "kz_dequantize_i8_f32": (_I, [_P, _I64, _D, _P, _P]),
     "kz_dequantize_cols_i8_f32": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "kz_qlinear_w8a32_f32": (_I, [_P, _I64, _I64, _P, _D, _P, _I64, _I, _P, _P]),
+    "kz_set_sm_count_target": (_I, [_I]),
     "kz_gemm_i8": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P]),
     "kz_gemm_i8_gated": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P, _P, _I64, _P, _P,
                               ctypes.c_uint32, _I, _I64, _P]),

@@ -771,7 +771,7 @@ struct TmapEntry {
     CUtensorMap a, b, out;
     bool valid;
 };
-constexpr int kTmapCache = 16;
+constexpr int kTmapCache = 64;   // a chunked, multi-layer forward cycles through dozens of (A, out) pairs
 thread_local TmapEntry t_tmap_cache[kTmapCache];
 thread_local int t_tmap_next = 0;
 
@@ -803,6 +803,9 @@ static int launch_gemm(int grid, cudaStream_t s, const TmapEntry* ent, const Gem
     }
     return KZ_OK;
 }
+
+// SM budget of the GEMMs per device (0: every SM), kz_set_sm_count_target.
+static std::atomic<int> g_sm_target[64];
 
 // How many CTA pairs of the pair kernel can be resident at once (cached per device).
 static int max_active_pairs(int dev) {
@@ -950,12 +953,15 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
     st = ensure_gemm_attrs(dev);
     if (st) return st;
 
+    const int target = dev >= 0 && dev < 64 ? g_sm_target[dev].load() : 0;
     int grid;
     if (pair) {
-        const int pairs = std::min(p.num_tiles, max_active_pairs(dev) - p.copy_ctas / 2);
+        int cap = max_active_pairs(dev);
+        if (target > 0) cap = std::max(1, std::min(cap, target / 2));
+        const int pairs = std::max(1, std::min(p.num_tiles, cap - p.copy_ctas / 2));
         grid = 2 * pairs;
     } else {
-        grid = std::min(p.num_tiles, sm_count());
+        grid = std::min(p.num_tiles, target > 0 ? std::min(target, sm_count()) : sm_count());
     }
     if (grid > KZ_PARTIALS_WORDS - 3 - p.copy_ctas) grid = (KZ_PARTIALS_WORDS - 3 - p.copy_ctas) & ~1;
     if (peers) {
@@ -982,6 +988,15 @@ static int gemm_i8_impl(const int8_t* A, const int8_t* B, int64_t M, int64_t N, 
     if (act == KZ_ACT_RELU) return launch_gemm<KZ_ACT_RELU, false>(grid, s, ent, p);
     if (act == KZ_ACT_GELU) return launch_gemm<KZ_ACT_GELU, false>(grid, s, ent, p);
     return launch_gemm<KZ_ACT_NONE, false>(grid, s, ent, p);
+}
+
+extern "C" int kz_set_sm_count_target(int sms) {
+    KZ_REQUIRE(sms >= 0, "kz_set_sm_count_target: sms must be >= 0");
+    int dev = 0;
+    KZ_CHECK_CUDA(cudaGetDevice(&dev));
+    KZ_REQUIRE(dev >= 0 && dev < 64, "kz_set_sm_count_target: device ordinal out of range");
+    g_sm_target[dev] = sms;
+    return KZ_OK;
 }
 
 extern "C" int kz_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, int64_t a_kblock,

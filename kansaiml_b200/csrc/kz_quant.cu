@@ -591,9 +591,10 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
         const int rows = (int)min((int64_t)kLnRows, M - r0);
         if (staged) {
             // rows in: ln_rows[r * stride + j] = x (+ res)
-            for (int64_t t = threadIdx.x; t < rows * D4; t += kLnThreads) {
-                const int r = (int)(t / D4);
-                const int64_t c = t - r * D4;
+            const int d4 = (int)D4;
+            for (int t = threadIdx.x; t < rows * d4; t += kLnThreads) {
+                const int r = t / d4;
+                const int c = t - r * d4;
                 const int64_t g = (r0 + r) * D4 + c;
                 float4 v = __ldg(reinterpret_cast<const float4*>(x) + g);
                 if (res) {
@@ -610,13 +611,15 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
             if (warp == 0 && lane < rows) {
                 const float4* row = reinterpret_cast<const float4*>(ln_rows + (int64_t)lane * stride);
                 float s = 0.0f;
-                for (int64_t c = 0; c < D4; ++c) {
+#pragma unroll 8
+                for (int c = 0; c < d4; ++c) {
                     const float4 v = row[c];
                     s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
                 }
                 const float mean = __fmul_rn(s, inv_d);
                 float q = 0.0f;
-                for (int64_t c = 0; c < D4; ++c) {
+#pragma unroll 8
+                for (int c = 0; c < d4; ++c) {
                     const float4 v = row[c];
                     const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean);
                     const float e = __fsub_rn(v.z, mean), f = __fsub_rn(v.w, mean);
@@ -629,9 +632,9 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
                 s_rden[lane] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(q, inv_d), eps)));
             }
             __syncthreads();
-            for (int64_t t = threadIdx.x; t < rows * D4; t += kLnThreads) {
-                const int r = (int)(t / D4);
-                const int64_t c = t - r * D4;
+            for (int t = threadIdx.x; t < rows * d4; t += kLnThreads) {
+                const int r = t / d4;
+                const int c = t - r * d4;
                 const float mean = s_mean[r], rden = s_rden[r];
                 const float4 v = *reinterpret_cast<const float4*>(ln_rows + (int64_t)r * stride + 4 * c);
                 const float4 gm = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + c) : make_float4(1.f, 1.f, 1.f, 1.f);
@@ -892,25 +895,34 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 
 // -------------------------------------------------------------- dequantize
 
-// Per-tensor dequantize through a 255-entry table: table[q + 127] =
+// Per-tensor dequantize through a lookup table: table[q + 127] =
 // (float)((double)q * scale) holds every value the reference can produce, so
-// the per-element work is one shared-memory lookup (1 B in, 4 B out).
+// the per-element work is one shared-memory load (1 B in, 4 B out).  The
+// table is replicated once per bank (entry e of copy b at word e * 32 + b) and
+// lane b reads copy b, so a warp's 32 lookups never conflict however the codes
+// fall.  Each thread converts 32 codes (two 16-byte loads in flight) per step.
+constexpr int kDeqTable = 256;
 __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restrict__ q, int64_t n, double scale,
                                                          float* __restrict__ out) {
-    __shared__ float table[256];
-    if (threadIdx.x < 255) table[threadIdx.x] = __double2float_rn((double)((int)threadIdx.x - 127) * scale);
-    if (threadIdx.x == 255) table[255] = __double2float_rn(-128.0 * scale);
+    __shared__ float table[kDeqTable * 32];
+    __shared__ float values[kDeqTable];
+    if (threadIdx.x < kDeqTable) {
+        const int e = threadIdx.x;   // e = q + 127; e == 255 holds q = -128
+        values[e] = __double2float_rn((double)(e == 255 ? -128 : e - 127) * scale);
+    }
     __syncthreads();
+    for (int i = threadIdx.x; i < kDeqTable * 32; i += blockDim.x) table[i] = values[i >> 5];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-    auto lut = [&](uint32_t byte) { return table[(((int)(int8_t)(uint8_t)byte) + 127) & 255]; };
+    auto lut = [&](uint32_t byte) { return table[(((((int)(int8_t)(uint8_t)byte) + 127) & 255) << 5) + lane]; };
     const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
     if (aligned) {
         const int64_t n16 = n >> 4;
         const uint4* qv = reinterpret_cast<const uint4*>(q);
         float4* ov = reinterpret_cast<float4*>(out);
-        for (int64_t i = tid; i < n16; i += nthreads) {
-            const uint4 c = __ldcs(qv + i);
+        auto emit = [&](const uint4& c, int64_t i) {
             const uint32_t w[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -921,7 +933,14 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
                 o.w = lut(w[j] >> 24);
                 __stcs(ov + 4 * i + j, o);
             }
+        };
+        int64_t i = tid;
+        for (; i + nthreads < n16; i += 2 * nthreads) {
+            const uint4 c0 = __ldcs(qv + i), c1 = __ldcs(qv + i + nthreads);
+            emit(c0, i);
+            emit(c1, i + nthreads);
         }
+        if (i < n16) emit(__ldcs(qv + i), i);
         for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
     } else {
         for (int64_t j = tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
@@ -1225,7 +1244,9 @@ int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, k
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    dequantize_kernel<<<elementwise_grid((n + 15) / 16), 256, 0, s>>>(q, n, scale, out);
+    // four resident blocks per SM (each builds its own 33 KB table once)
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 32 * 256 - 1) / (32 * 256), 4 * (int64_t)sm_count()));
+    dequantize_kernel<<<grid, 256, 0, s>>>(q, n, scale, out);
     return launch_status("dequantize_kernel");
 }
 

@@ -468,6 +468,65 @@ class _PeerGather:
         self.own, self.xflags, self.peer, self.peer_xflags = [], [], [], []
 
 
+def pipeline_chunks(M, world):
+    """Row chunks C of the sharded stack's pipelined exchange for an M-row
+    batch: 1 on one GPU; otherwise the first of 4, 2, 1 that splits M into C x
+    world equal row blocks with chunks of at least 256 rows; 0 when none
+    does (the stack then takes its unpipelined forward)."""
+    if world == 1:
+        return 1
+    for c in (4, 2, 1):
+        if M % (c * world) == 0 and (c == 1 or M // c >= 256):
+            return c
+    return 0
+
+
+def pipeline_input_rows(M, world, rank):
+    """Rank `rank`'s rows of an [M, K] input in the pipelined layout, as
+    [(start, stop)]: in each of the C row chunks (M / C rows) the rank owns
+    the rank-th block of M / (C x world) rows, so the all-gather of chunk c
+    lands the quantized input's rows in natural order."""
+    C = pipeline_chunks(M, world)
+    if C == 0:
+        raise ValueError(f"{M} rows do not split into equal blocks over {world} ranks")
+    mc = M // C
+    mp = mc // world
+    return [(c * mc + rank * mp, c * mc + (rank + 1) * mp) for c in range(C)]
+
+
+class _PhaseEvents:
+    """CUDA events around the phases of a forward on the current stream
+    (only when enabled).  ``finish()`` synchronises and returns
+    {phase: milliseconds}, summed over the phase's intervals; a phase that
+    waits for an all-gather measures the stall the stream actually saw."""
+
+    def __init__(self, enabled, dev):
+        self.enabled, self.dev = enabled, dev
+        self.marks, self.open = [], None
+
+    def begin(self, name):
+        if self.enabled:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(torch.cuda.current_stream(self.dev))
+            self.open = (name, e)
+
+    def end(self):
+        if self.enabled and self.open is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(torch.cuda.current_stream(self.dev))
+            self.marks.append((self.open[0], self.open[1], e))
+            self.open = None
+
+    def finish(self):
+        if not self.enabled:
+            return None
+        torch.cuda.synchronize(self.dev)
+        out = {}
+        for name, a, b in self.marks:
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
 class ShardedQLinearStack:
     """A stack of bias-free int8 Linear layers, weights column-sharded over the
     ranks of an SPMD mesh (or a single GPU when the mesh is None).
@@ -513,6 +572,9 @@ class ShardedQLinearStack:
         self.exchange = exchange if self.world > 1 else "collective"
         self.copy_ctas = 8
         self._peer = None
+        self._bufs = {}
+        self.timing = False        # record per-phase CUDA-event times in forward_local (phase_times)
+        self._phases = None
 
     def close(self):
         """Release the peer exchange buffers (collective over the mesh)."""
@@ -520,11 +582,130 @@ class ShardedQLinearStack:
             self._peer.close()
             self._peer = None
 
+    # ------------------------------------------------- pipelined forward
+
+    def chunks(self, M):
+        """Row chunks of the pipelined exchange (pipeline_chunks)."""
+        return pipeline_chunks(M, self.world)
+
+    def input_rows(self, M):
+        """This rank's rows of an [M, K] input in the pipelined layout (pipeline_input_rows)."""
+        return pipeline_input_rows(M, self.world, self.rank)
+
+    def local_input(self, x):
+        """This rank's rows (input_rows) of a replicated [M, K] input, stacked."""
+        xd = as_tensor(x).data
+        return torch.cat([xd[a:b] for a, b in self.input_rows(xd.shape[0])]).contiguous()
+
+    def _zeroed(self, key, shape, dtype, dev):
+        buf = self._bufs.get(key)
+        if buf is None or buf.device != dev or tuple(buf.shape) != tuple(shape):
+            buf = torch.zeros(shape, dtype=dtype, device=dev)
+            self._bufs[key] = buf
+        return buf
+
+    def forward_local(self, x_local, M):
+        """The stack on this rank's input rows (local_input / input_rows
+        layout, fp32 [M / world, K]).  Returns this rank's fp32 column shard
+        of the last layer's output, [M, N / world].
+
+        Pipelined over C row chunks: each layer's int8 activations travel as
+        C NCCL all-gathers (async, on the process group's stream), and the
+        next layer's GEMM runs chunk by chunk, each chunk waiting (stream
+        order, no spinning) only for its own all-gather, so the all-gather of
+        chunk c + 1 overlaps the GEMM of chunk c.  The per-tensor scale needs
+        the whole layer's absmax first: the GEMM epilogues write absmax
+        partials per chunk, combined and MAX-all-reduced once per layer."""
+        xd = as_tensor(x_local).data
+        dev = xd.device
+        G, C = self.world, self.chunks(M)
+        mc = M // C
+        mp = mc // G
+        if xd.shape[0] != C * mp:
+            raise ValueError(f"local input has {xd.shape[0]} rows, expected {C * mp}")
+        ev = _PhaseEvents(self.timing, dev)
+        # layer-0 input: absmax of the local rows -> global absmax -> local codes
+        ev.begin("input_quantize")
+        parts = self._zeroed("in_parts", (_lib.KZ_PARTIALS_WORDS,), torch.int32, dev)
+        _lib.call("kz_absmax_f32", ptr(xd), xd.numel(), ptr(parts), stream_handle(dev))
+        if G > 1:
+            allreduce_partials_max(parts, self.group)
+        codes, _, a_s32 = quantize_partials_device(xd, parts)
+        ev.end()
+        K0 = self.layers[0][1]
+        works = [None] * C
+        if G > 1:
+            A = torch.empty((M, K0), dtype=torch.int8, device=dev)
+            for c in range(C):
+                works[c] = dist.all_gather_into_tensor(A[c * mc:(c + 1) * mc], codes[c * mp:(c + 1) * mp],
+                                                       group=self.group, async_op=True)
+        else:
+            A = codes
+        a_chunks = [(A[c * mc:(c + 1) * mc], K0) for c in range(C)]
+        y = None
+        for li, (qt, K, N) in enumerate(self.layers):
+            n_loc = qt.shape[1]
+            last = li == len(self.layers) - 1
+            y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
+            pb = None if last else self._zeroed(("chunk_parts", C), (C, _lib.KZ_PARTIALS_WORDS), torch.int32, dev)
+            for c in range(C):
+                if works[c] is not None:
+                    ev.begin("wait_allgather")
+                    works[c].wait()
+                    ev.end()
+                a, kb = a_chunks[c]
+                ev.begin("gemm")
+                gemm_i8_device(a, qt.kmajor(), row_scale=a_s32, col_scale=qt.scale_f32, a_kblock=kb, m=mc,
+                               out=y[c * mc:(c + 1) * mc], partials=None if last else pb[c])
+                ev.end()
+            if last:
+                break
+            ev.begin("allreduce_max")
+            lp = torch.amax(pb, 0) if C > 1 else pb[0]
+            if G > 1:
+                allreduce_partials_max(lp, self.group)
+            ev.end()
+            ev.begin("quantize")
+            yq = torch.empty((M, n_loc), dtype=torch.int8, device=dev)
+            s64 = torch.empty(1, dtype=torch.float64, device=dev)
+            a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
+            gathered = torch.empty((C, G, mc, n_loc), dtype=torch.int8, device=dev) if G > 1 else None
+            for c in range(C):
+                rows = slice(c * mc, (c + 1) * mc)
+                _lib.call("kz_quantize_partials_f32", ptr(y[rows]), mc * n_loc, ptr(lp), ptr(yq[rows]), ptr(s64),
+                          ptr(a_s32), stream_handle(dev))
+                if G > 1:
+                    works[c] = dist.all_gather_into_tensor(gathered[c], yq[rows], group=self.group, async_op=True)
+            ev.end()
+            a_chunks = [(gathered[c], n_loc) for c in range(C)] if G > 1 else [(yq, N)]
+        self._phases = ev
+        return Tensor(y)
+
+    def phase_times(self):
+        """{phase: ms} of the last forward_local run with ``timing`` on
+        (synchronises the device), else None."""
+        return self._phases.finish() if self._phases is not None else None
+
     def forward(self, x, return_local=True):
         """x: fp32 [M, K] replicated on every rank.  Returns the last layer's
         fp32 output: this rank's column shard (return_local) or the full
-        [M, N] (all-gathered)."""
+        [M, N] (all-gathered).  With the collective exchange and M splitting
+        into equal row blocks, each rank quantizes and all-gathers only its
+        own rows of x (forward_local); otherwise every rank quantizes all of x."""
         xd = as_tensor(x).data.contiguous()
+        M = xd.shape[0]
+        if self.exchange == "collective" and self.chunks(M) > 0:
+            y = self.forward_local(self.local_input(xd) if self.world > 1 else xd, M).data
+        else:
+            y = self._forward_replicated(xd)
+        if return_local or self.world == 1:
+            return Tensor(y)
+        parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
+        return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+
+    def _forward_replicated(self, xd):
+        """Every rank quantizes the whole replicated input; one all-gather per
+        layer boundary (or the peer / fused exchanges)."""
         dev = xd.device
         if self.partials is None or self.partials.device != dev:
             self.partials = new_partials(dev)
@@ -568,10 +749,7 @@ class ShardedQLinearStack:
             else:
                 a = yq
                 a_kblock = N
-        if return_local or self.world == 1:
-            return Tensor(y)
-        parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
-        return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+        return y
 
     def _gemm_fused(self, gate, M, K, qt, a_s32, partials):
         a_ptr, peer_a, peer_f, flags, token = gate

@@ -259,3 +259,33 @@ def test_gather_row_chunk_properties(m128):
     rows = _row_chunk(M)
     assert rows % 128 == 0 and M % rows == 0 and M // rows <= 8
     assert all(M % r or M // r > 8 for r in range(128, rows, 128))
+
+
+@settings(max_examples=60, deadline=None)
+@given(st.integers(1, 40), st.sampled_from([1, 2, 4, 8]))
+def test_pipeline_input_rows_tile_the_batch_in_gather_order(m_blocks, world):
+    """Every row of the batch belongs to exactly one rank, each rank owns the
+    same count, and concatenating chunk c's blocks in rank order (what the
+    all-gather of chunk c produces) walks rows c * M / C .. in natural order."""
+    from kansaiml_b200.distributed import pipeline_chunks, pipeline_input_rows
+    M = 64 * m_blocks * world
+    C = pipeline_chunks(M, world)
+    assert C >= 1 and M % (C * world) == 0
+    per_rank = [pipeline_input_rows(M, world, r) for r in range(world)]
+    assert all(len(p) == C for p in per_rank)
+    order = []
+    for c in range(C):
+        for r in range(world):
+            a, b = per_rank[r][c]
+            order.extend(range(a, b))
+    assert order == list(range(M))
+    assert len({sum(b - a for a, b in p) for p in per_rank}) == 1
+
+
+def test_pipeline_chunks_rejects_uneven_batches():
+    from kansaiml_b200.distributed import pipeline_chunks, pipeline_input_rows
+    assert pipeline_chunks(8192, 8) == 4 and pipeline_chunks(8192, 1) == 1
+    assert pipeline_chunks(384, 2) == 1 or 384 // pipeline_chunks(384, 2) >= 256
+    assert pipeline_chunks(1001, 2) == 0
+    with pytest.raises(ValueError):
+        pipeline_input_rows(1001, 2, 0)

@@ -27,8 +27,8 @@ def make_weights():
     return [(rs.standard_normal((DIMS[i], DIMS[i + 1])) * 0.01).astype(np.float32) for i in range(len(DIMS) - 1)]
 
 
-def make_x():
-    return np.random.RandomState(56).standard_normal((M, DIMS[0])).astype(np.float32)
+def make_x(m=M):
+    return np.random.RandomState(56).standard_normal((m, DIMS[0])).astype(np.float32)
 
 
 def oracle_chain(x, weights):
@@ -108,6 +108,94 @@ def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
     for r in range(2):
         assert isinstance(res[r], np.ndarray), res[r]
         assert res[r].tobytes() == expected.tobytes()
+
+
+M_PIPE = 2048   # four row chunks of 512 on two ranks
+
+
+def _pipelined_worker(rank, world, port, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from kansaiml_b200 import _lib
+        from kansaiml_b200 import distributed as kd
+        mesh = kd.DeviceMesh.spmd()
+        stack = kd.ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh)
+        assert stack.chunks(M_PIPE) == 4
+        x = torch.from_numpy(make_x(M_PIPE)).cuda()
+        full = stack(x, return_local=False).numpy()
+        # the same forward replayed from a CUDA graph (NCCL all-gathers and
+        # all-reduces captured), with the GEMMs' SM budget cut for the overlap
+        assert _lib.load().kz_set_sm_count_target(100) == 0
+        xl = stack.local_input(x)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            out = stack.forward_local(xl, M_PIPE)
+        g.replay()
+        g.replay()
+        torch.cuda.synchronize()
+        lo, hi = kd.column_shard_bounds(DIMS[-1], rank, world)
+        graphed = out.data.cpu().numpy()
+        ok = graphed.tobytes() == np.ascontiguousarray(full[:, lo:hi]).tobytes()
+        # per-phase timing path
+        stack.timing = True
+        stack.forward_local(xl, M_PIPE)
+        phases = stack.phase_times()
+        stack.timing = False
+        ok = ok and set(phases) >= {"gemm", "input_quantize", "quantize", "allreduce_max"}
+        # dtensor_grad over NCCL: Replicate -> all-reduce sum in the
+        # reference's double order, Shard(0) -> concatenation
+        local = torch.full((3, 2), float(rank + 1), device="cuda") / 3
+        rep, sh = kd.dtensor_grad(lambda t: (t, t * 2), [kd.Replicate(), kd.Shard(0)],
+                                  kd.DTensor(mesh, kd.Shard(0), [kz_tensor(local)]))
+        want_rep = np.float32(sum(np.float64(np.float32((r + 1) / 3)) for r in range(world)))
+        ok = ok and np.all(rep.numpy() == want_rep)
+        ok = ok and sh.shape == [3 * world, 2]
+        from kansaiml_b200.quantize import device_status
+        assert device_status() == 0
+        del g
+        q.put((rank, full if ok else "graph replay, phases or dtensor_grad differ"))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+def kz_tensor(t):
+    from kansaiml_b200.tensor import Tensor
+    return Tensor(t)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_stack_pipelined_two_gpus_graph_and_grad():
+    """Two ranks, 2048 rows in four row chunks: the pipelined forward (input
+    rows quantized per rank and all-gathered chunk by chunk, every layer's
+    codes all-gathered chunk by chunk under the next GEMM) equals the oracle's
+    unsharded chain bit for bit, also when replayed from a CUDA graph that
+    captured its NCCL collectives; dtensor_grad's NCCL reductions match the
+    reference's double-precision sum."""
+    expected_pipe = oracle_chain(make_x(M_PIPE), make_weights())
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pipelined_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, y = q.get(timeout=300)
+        res[r] = y
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert isinstance(res[r], np.ndarray), res[r]
+        assert res[r].tobytes() == expected_pipe.tobytes()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
