@@ -77,9 +77,11 @@ def parse():
     ap.add_argument("--exchange", choices=["peer", "collective", "fused"], default=None,
                     help="stack: pipelined NCCL all-gathers (collective, default), copy-engine pulls feeding the "
                          "gated GEMM (peer) or the all-gather inside the GEMM launch (fused)")
-    ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp", "kernels", "gemm"],
+                    default="stack",
                     help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
-                         "mlp: config 1")
+                         "mlp: config 1; kernels: the per-kernel entries alone; gemm: one GEMM shape (--shape)")
+    ap.add_argument("--shape", default="8192,16384,16384", help="gemm workload: M,N,K")
     return ap.parse_args()
 
 
@@ -628,7 +630,8 @@ def measure_kernels(args, rank, world, local_rank, dev):
     hbm_gbs, bf16, _, peak_src = peaks()
     int8_peak = 2.0 * bf16
     out = {}
-    out["config2_linear"] = measure_linear(args, rank, world, local_rank, dev, steps=400, with_e2e=False)
+    out["config2_linear"] = measure_linear(args, rank, world, local_rank, dev, steps=max(8, 4 * args.steps),
+                                           with_e2e=False)
     torch.cuda.empty_cache()
     i = [0]
 
@@ -817,6 +820,15 @@ def run_stack(args, rank, world, local_rank, dev):
         ms = float(t.item())
     ms_per_step = ms / K
     status = device_status()
+    # A checksum of the whole output (the int32 bit patterns of every rank's
+    # column shard, summed): sharding changes no arithmetic, so it is the same
+    # number at every N when the sharded forward is bit-identical to N = 1.
+    y_chk = fwd().data
+    chk = y_chk.view(torch.int32).to(torch.int64).sum().reshape(1)
+    if world > 1:
+        dist.all_reduce(chk)
+    checksum = f"{int(chk.item()) & 0xFFFFFFFFFFFFFFFF:016x}"
+    del y_chk
 
     # per-phase device times of one eager forward (events on the compute stream)
     phases = None
@@ -913,6 +925,9 @@ def run_stack(args, rank, world, local_rank, dev):
                      "timing": f"CUDA events around 4 replays of a graph of the step's {4 * C} GEMM launches "
                                "(same shapes and weights) alone, right after the timed region"},
         "phases_ms": phases,
+        "output_checksum": checksum,
+        "output_checksum_note": "sum of the int32 bit patterns of the full fp32 output over all ranks; equal at "
+                                "every N when the sharded forward is bit-identical to the one-GPU forward",
         "device_status": status,
         "e2e": e2e,
         "cpu_baseline": cpu,
@@ -1070,6 +1085,48 @@ def run_mlp(args, rank, world, local_rank, dev):
     print(json.dumps(line))
 
 
+def run_kernels(args, rank, world, local_rank, dev):
+    """The per-kernel entries of the default line on their own (N = 1)."""
+    k = measure_kernels(args, rank, world, local_rank, dev)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "workload": "per-kernel entries (N = 1)", "kernels": k}))
+
+
+def run_gemm(args, rank, world, local_rank, dev):
+    """A few launches of the int8 GEMM at one shape (--shape M,N,K), fp32
+    epilogue with per-row x per-column scales and absmax partials, as the
+    sharded stack launches it: a profiling target."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    M, N, K = (int(v) for v in args.shape.split(","))
+    g = torch.Generator(device=dev)
+    g.manual_seed(M + N + K)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+    rs_ = torch.full((1,), 1e-3, device=dev)
+    cs_ = torch.rand(N, device=dev, generator=g) * 9e-3 + 1e-3
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    parts = torch.zeros(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+
+    def call():
+        _ok(lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), M, N, K, K, rs_.data_ptr(), 0, cs_.data_ptr(), 1, None, 0,
+                           y.data_ptr(), None, N, parts.data_ptr(), _sh(dev)))
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    start, end = _events(dev)
+    start.record(torch.cuda.current_stream(dev))
+    for _ in range(args.steps):
+        call()
+    end.record(torch.cuda.current_stream(dev))
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) / args.steps * 1e3
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "workload": f"int8 GEMM M={M} N={N} K={K}", "avg_us": us,
+                          "tops": 2.0 * M * N * K / (us / 1e6) / 1e12, "launches": args.steps + max(args.warmup, 1)}))
+
+
 # ------------------------------------------------------------------- main
 
 def main():
@@ -1099,7 +1156,7 @@ def main():
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
     {"stack": run_stack, "linear": run_linear, "transformer": run_transformer, "sweep": run_sweep,
-     "mlp": run_mlp}[args.workload](args, rank, world, local_rank, dev)
+     "mlp": run_mlp, "kernels": run_kernels, "gemm": run_gemm}[args.workload](args, rank, world, local_rank, dev)
 
 
 if __name__ == "__main__":

@@ -42,6 +42,9 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int EPI_WARPS = 8;                         // two per TMEM sub-partition, one per column half
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
+#ifndef KZ_EPI_DIRECT
+#define KZ_EPI_DIRECT 0   // 1: epilogue stores straight from registers (32-byte stores) instead of TMA
+#endif
 constexpr int GROUP_M = 16;        // tile rasterisation: 16 tile-rows per group
 constexpr int EPI_BUF = 32 * 32 * 4;                 // one warp's 32 x 32 fp32/int32 sub-tile
 constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;       // one staging buffer per warp: 32 KB
@@ -570,7 +573,24 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = r[j];
                 }
-                if (p.tma_out) {
+                if (p.tma_out && KZ_EPI_DIRECT) {
+                    // each lane writes its row's 32 values as four 32-byte stores (whole sectors)
+                    if (row_ok) {
+                        uint32_t* dst = (p.out_f32 ? reinterpret_cast<uint32_t*>(p.out_f32)
+                                                   : reinterpret_cast<uint32_t*>(p.out_i32)) +
+                                        (int64_t)m * p.ldo + nb;
+                        if (nb + 32 <= p.N && p.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + 8 * j),
+                                             "r"(v[8 * j]), "r"(v[8 * j + 1]), "r"(v[8 * j + 2]), "r"(v[8 * j + 3]),
+                                             "r"(v[8 * j + 4]), "r"(v[8 * j + 5]), "r"(v[8 * j + 6]), "r"(v[8 * j + 7])
+                                             : "memory");
+                        } else {
+                            for (int j = 0; j < 32 && nb + j < p.N; ++j) dst[j] = v[j];
+                        }
+                    }
+                } else if (p.tma_out) {
                     // stage the warp's 32 x 32 sub-tile (128-byte rows, 128B-swizzled) and TMA-store it
                     const uint32_t buf = epi0;
                     if (qchunk >= 1) {

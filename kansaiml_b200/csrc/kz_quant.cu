@@ -573,6 +573,7 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
 // arithmetic reads global memory directly.
 constexpr int kLnRows = 32;
 constexpr int kLnThreads = 256;
+constexpr int kLnBatch = 8;   // 16-byte loads in flight per thread while staging rows
 
 __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
     const float* __restrict__ x, int64_t M, int64_t D, const float* __restrict__ gamma,
@@ -590,22 +591,39 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
     for (int64_t r0 = (int64_t)blockIdx.x * kLnRows; r0 < M; r0 += (int64_t)gridDim.x * kLnRows) {
         const int rows = (int)min((int64_t)kLnRows, M - r0);
         if (staged) {
-            // rows in: ln_rows[r * stride + j] = x (+ res)
+            // rows in: ln_rows[r * stride + j] = x (+ res); batches of kLnBatch
+            // 16-byte loads per thread are issued before any is used
             const int d4 = (int)D4;
-            for (int t = threadIdx.x; t < rows * d4; t += kLnThreads) {
-                const int r = t / d4;
-                const int c = t - r * d4;
-                const int64_t g = (r0 + r) * D4 + c;
-                float4 v = __ldg(reinterpret_cast<const float4*>(x) + g);
-                if (res) {
-                    const float4 w = __ldg(reinterpret_cast<const float4*>(res) + g);
-                    v.x = __fadd_rn(v.x, w.x);
-                    v.y = __fadd_rn(v.y, w.y);
-                    v.z = __fadd_rn(v.z, w.z);
-                    v.w = __fadd_rn(v.w, w.w);
-                    reinterpret_cast<float4*>(sum_out)[g] = v;
+            const int total = rows * d4;
+            const float4* x4 = reinterpret_cast<const float4*>(x) + r0 * D4;
+            const float4* res4 = res ? reinterpret_cast<const float4*>(res) + r0 * D4 : nullptr;
+            for (int t0 = threadIdx.x; t0 < total; t0 += kLnThreads * kLnBatch) {
+                float4 v[kLnBatch], w[kLnBatch];
+#pragma unroll
+                for (int u = 0; u < kLnBatch; ++u) {
+                    const int t = t0 + u * kLnThreads;
+                    if (t < total) {
+                        v[u] = __ldg(x4 + t);
+                        if (res4) w[u] = __ldg(res4 + t);
+                    }
                 }
-                *reinterpret_cast<float4*>(ln_rows + (int64_t)r * stride + 4 * c) = v;
+#pragma unroll
+                for (int u = 0; u < kLnBatch; ++u) {
+                    const int t = t0 + u * kLnThreads;
+                    if (t < total) {
+                        const int r = t / d4;
+                        const int c = t - r * d4;
+                        float4 a = v[u];
+                        if (res4) {
+                            a.x = __fadd_rn(a.x, w[u].x);
+                            a.y = __fadd_rn(a.y, w[u].y);
+                            a.z = __fadd_rn(a.z, w[u].z);
+                            a.w = __fadd_rn(a.w, w[u].w);
+                            reinterpret_cast<float4*>(sum_out)[r0 * D4 + t] = a;
+                        }
+                        *reinterpret_cast<float4*>(ln_rows + (int64_t)r * stride + 4 * c) = a;
+                    }
+                }
             }
             __syncthreads();
             if (warp == 0 && lane < rows) {
