@@ -55,8 +55,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .quantize import (QTensor, gemm_i8_device, new_partials, quantize_cols_device, quantize_partials_device,
-                       quantize_tensor_device)
+from .quantize import (QTensor, absmax_partials_device, gemm_i8_device, new_partials, quantize_cols_device,
+                       quantize_partials_device, quantize_tensor_device)
 from .tensor import ptr, stream_handle
 from .tensor import Tensor, as_tensor, cat
 
@@ -351,6 +351,15 @@ def allgather_blocked(local, group=None, out=None):
     return out
 
 
+def _all_gather_async(out, local, group=None):
+    """Async all-gather of equally shaped shards into out[G, *local.shape]
+    (rank-major); returns the work handle, whose wait() makes the current
+    stream wait for it (NCCL) or blocks until done (gloo)."""
+    if dist.get_backend(group) == "nccl":
+        return dist.all_gather_into_tensor(out, local, group=group, async_op=True)
+    return dist.all_gather(list(out.unbind(0)), local, group=group, async_op=True)
+
+
 def column_shard_bounds(total, rank, world):
     """[start, stop) of this rank's columns under Shard(1) (remainder first)."""
     sizes = _chunk_sizes(total, world)
@@ -627,7 +636,7 @@ class ShardedQLinearStack:
         # layer-0 input: absmax of the local rows -> global absmax -> local codes
         ev.begin("input_quantize")
         parts = self._zeroed("in_parts", (_lib.KZ_PARTIALS_WORDS,), torch.int32, dev)
-        _lib.call("kz_absmax_f32", ptr(xd), xd.numel(), ptr(parts), stream_handle(dev))
+        absmax_partials_device(xd, parts)
         if G > 1:
             allreduce_partials_max(parts, self.group)
         codes, _, a_s32 = quantize_partials_device(xd, parts)
@@ -637,8 +646,8 @@ class ShardedQLinearStack:
         if G > 1:
             A = torch.empty((M, K0), dtype=torch.int8, device=dev)
             for c in range(C):
-                works[c] = dist.all_gather_into_tensor(A[c * mc:(c + 1) * mc], codes[c * mp:(c + 1) * mp],
-                                                       group=self.group, async_op=True)
+                works[c] = _all_gather_async(A[c * mc:(c + 1) * mc].view(G, mp, K0), codes[c * mp:(c + 1) * mp],
+                                             self.group)
         else:
             A = codes
         a_chunks = [(A[c * mc:(c + 1) * mc], K0) for c in range(C)]
@@ -672,10 +681,9 @@ class ShardedQLinearStack:
             gathered = torch.empty((C, G, mc, n_loc), dtype=torch.int8, device=dev) if G > 1 else None
             for c in range(C):
                 rows = slice(c * mc, (c + 1) * mc)
-                _lib.call("kz_quantize_partials_f32", ptr(y[rows]), mc * n_loc, ptr(lp), ptr(yq[rows]), ptr(s64),
-                          ptr(a_s32), stream_handle(dev))
+                quantize_partials_device(y[rows], lp, q=yq[rows], s64=s64, s32=a_s32)
                 if G > 1:
-                    works[c] = dist.all_gather_into_tensor(gathered[c], yq[rows], group=self.group, async_op=True)
+                    works[c] = _all_gather_async(gathered[c], yq[rows], self.group)
             ev.end()
             a_chunks = [(gathered[c], n_loc) for c in range(C)] if G > 1 else [(yq, N)]
         self._phases = ev

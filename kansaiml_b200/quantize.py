@@ -80,11 +80,18 @@ def quantize_tensor_device(x):
     return q, s64, s32
 
 
-def quantize_partials_device(x, partials):
+def quantize_partials_device(x, partials, q=None, s64=None, s32=None):
+    """Per-tensor quantize of a contiguous fp32 CUDA tensor with the absmax
+    given by `partials` (kz_quantize_partials_f32).  Writes into q / s64 / s32
+    when given (e.g. one row chunk of a larger code buffer).  Returns
+    (codes int8 like x, scale float64[1], scale float32[1])."""
     dev = x.device
-    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
-    s64 = torch.empty(1, dtype=torch.float64, device=dev)
-    s32 = torch.empty(1, dtype=torch.float32, device=dev)
+    if q is None:
+        q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    if s64 is None:
+        s64 = torch.empty(1, dtype=torch.float64, device=dev)
+    if s32 is None:
+        s32 = torch.empty(1, dtype=torch.float32, device=dev)
     _lib.call("kz_quantize_partials_f32", ptr(x), x.numel(), ptr(partials), ptr(q), ptr(s64), ptr(s32),
               stream_handle(dev))
     return q, s64, s32

@@ -289,3 +289,112 @@ def test_pipeline_chunks_rejects_uneven_batches():
     assert pipeline_chunks(1001, 2) == 0
     with pytest.raises(ValueError):
         pipeline_input_rows(1001, 2, 0)
+
+
+# ----------------------- the pipelined sharded stack's data movement on gloo
+
+PIPE_DIMS, PIPE_M = [256, 512, 256, 256], 1024   # four row chunks on two ranks
+
+
+def _pipe_weights():
+    rs = np.random.RandomState(81)
+    return [(rs.standard_normal((PIPE_DIMS[i], PIPE_DIMS[i + 1])) * 0.05).astype(np.float32)
+            for i in range(len(PIPE_DIMS) - 1)]
+
+
+def _pipe_x():
+    return np.random.RandomState(82).standard_normal((PIPE_M, PIPE_DIMS[0])).astype(np.float32)
+
+
+def _install_cpu_kernels():
+    """The stack's four device primitives, restated on the CPU through the
+    oracle with the same contracts (absmax partials words, per-tensor
+    quantize from partials, blocked-A int8 GEMM with fused epilogue and output
+    absmax), so the pipelined forward's chunking, row ownership and gather
+    layouts run on gloo ranks without a GPU."""
+    from oracle import cpu as ocpu
+
+    def put_absmax(partials, value):
+        partials[0] = 1
+        partials[1] = int(np.asarray([value], np.float32).view(np.int32)[0])
+
+    def absmax_from(partials):
+        n = int(partials[0])
+        return float(partials[1:1 + n].numpy().view(np.float32).max()) if n else 0.0
+
+    def quantize_cols_cpu(w):
+        qT, s = ocpu.quantize_cols(w.numpy())
+        return torch.from_numpy(qT), torch.from_numpy(s), torch.from_numpy(s.astype(np.float32))
+
+    def absmax_cpu(x, partials=None):
+        put_absmax(partials, np.abs(x.numpy()).max())
+        return partials
+
+    def quantize_partials_cpu(x, partials, q=None, s64=None, s32=None):
+        codes, scale = ocpu.quantize_with_absmax(x.numpy(), absmax_from(partials))
+        q = torch.empty(x.shape, dtype=torch.int8) if q is None else q
+        s64 = torch.empty(1, dtype=torch.float64) if s64 is None else s64
+        s32 = torch.empty(1, dtype=torch.float32) if s32 is None else s32
+        q.copy_(torch.from_numpy(codes))
+        s64.fill_(scale)
+        s32.fill_(float(np.float32(scale)))
+        return q, s64, s32
+
+    def gemm_cpu(a, b, row_scale=None, col_scale=None, a_kblock=None, m=None, out=None, partials=None, **_):
+        N, K = b.shape
+        kb = a_kblock or K
+        a2 = a.reshape(K // kb, m, kb).permute(1, 0, 2).reshape(m, K).numpy()
+        y = ocpu.epilogue(ocpu.gemm_i8(a2, b.numpy()), row_scale.numpy()[0], col_scale.numpy())
+        out.copy_(torch.from_numpy(y))
+        if partials is not None:
+            put_absmax(partials, np.abs(y).max())
+        return out, None
+
+    kd.quantize_cols_device = quantize_cols_cpu
+    kd.absmax_partials_device = absmax_cpu
+    kd.quantize_partials_device = quantize_partials_cpu
+    kd.gemm_i8_device = gemm_cpu
+
+
+def _pipe_worker(rank, world, port, q):
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        _install_cpu_kernels()
+        mesh = kd.DeviceMesh.spmd() if world > 1 else None
+        stack = kd.ShardedQLinearStack([torch.from_numpy(w) for w in _pipe_weights()], mesh)
+        assert stack.chunks(PIPE_M) == (4 if world > 1 else 1)
+        y = stack(torch.from_numpy(_pipe_x()), return_local=False).numpy()
+        q.put((rank, y))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+def test_pipelined_stack_world2_gloo_matches_oracle_chain():
+    """Two gloo ranks run the pipelined forward (input rows quantized per rank
+    and all-gathered in four row chunks, each layer's codes all-gathered in
+    chunks into [C][G][M/C][N/G] blocks) over CPU restatements of the device
+    primitives: the gathered output equals the oracle's unsharded chain."""
+    from oracle import cpu as ocpu
+    a, s_a = ocpu.quantize_tensor(_pipe_x())
+    want = None
+    for i, w in enumerate(_pipe_weights()):
+        wq, ws = ocpu.quantize_cols(w)
+        want = ocpu.epilogue(ocpu.gemm_i8(a, wq), s_a, ws)
+        if i < len(PIPE_DIMS) - 2:
+            a, s_a = ocpu.quantize_tensor(want)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pipe_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, y = q.get(timeout=240)
+        res[r] = y
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert isinstance(res[r], np.ndarray), res[r]
+        assert res[r].tobytes() == want.tobytes()
