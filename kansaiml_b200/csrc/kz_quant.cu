@@ -571,8 +571,8 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
 // quarter-warp hit distinct bank groups), and finally all threads write y with
 // coalesced 16-byte stores and take its absmax.  Otherwise the same
 // arithmetic reads global memory directly.
-constexpr int kLnRows = 32;
-constexpr int kLnThreads = 256;
+constexpr int kLnRows = 16;
+constexpr int kLnThreads = 128;
 constexpr int kLnBatch = 8;   // 16-byte loads in flight per thread while staging rows
 
 __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
@@ -918,8 +918,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 // the per-element work is one shared-memory load (1 B in, 4 B out).  The
 // table is replicated once per bank (entry e of copy b at word e * 32 + b) and
 // lane b reads copy b, so a warp's 32 lookups never conflict however the codes
-// fall.  Each thread converts 32 codes (two 16-byte loads in flight) per step.
+// fall.  Thread t turns one 4-byte word of codes into one 16-byte store, so
+// warps read and write contiguous runs; each thread loads kDeqBatch words
+// before converting any.
 constexpr int kDeqTable = 256;
+constexpr int kDeqBatch = 8;   // 4-byte code words in flight per thread
 __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restrict__ q, int64_t n, double scale,
                                                          float* __restrict__ out) {
     __shared__ float table[kDeqTable * 32];
@@ -935,31 +938,30 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
     auto lut = [&](uint32_t byte) { return table[(((((int)(int8_t)(uint8_t)byte) + 127) & 255) << 5) + lane]; };
-    const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+    const bool aligned = (reinterpret_cast<uintptr_t>(q) & 3u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
     if (aligned) {
-        const int64_t n16 = n >> 4;
-        const uint4* qv = reinterpret_cast<const uint4*>(q);
+        // thread t converts word t of 4 codes into one 16-byte store, so a
+        // warp reads 128 contiguous bytes and writes 512; kDeqBatch words
+        // per thread are loaded before any is converted
+        const int64_t n4 = n >> 2;
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
         float4* ov = reinterpret_cast<float4*>(out);
-        auto emit = [&](const uint4& c, int64_t i) {
-            const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        for (int64_t i0 = tid; i0 < n4; i0 += kDeqBatch * nthreads) {
+            uint32_t w[kDeqBatch];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float4 o;
-                o.x = lut(w[j] & 0xFF);
-                o.y = lut((w[j] >> 8) & 0xFF);
-                o.z = lut((w[j] >> 16) & 0xFF);
-                o.w = lut(w[j] >> 24);
-                __stcs(ov + 4 * i + j, o);
+            for (int u = 0; u < kDeqBatch; ++u) {
+                const int64_t i = i0 + u * nthreads;
+                w[u] = i < n4 ? __ldcs(qw + i) : 0u;
             }
-        };
-        int64_t i = tid;
-        for (; i + nthreads < n16; i += 2 * nthreads) {
-            const uint4 c0 = __ldcs(qv + i), c1 = __ldcs(qv + i + nthreads);
-            emit(c0, i);
-            emit(c1, i + nthreads);
+#pragma unroll
+            for (int u = 0; u < kDeqBatch; ++u) {
+                const int64_t i = i0 + u * nthreads;
+                if (i < n4)
+                    __stcs(ov + i, make_float4(lut(w[u] & 0xFF), lut((w[u] >> 8) & 0xFF), lut((w[u] >> 16) & 0xFF),
+                                               lut(w[u] >> 24)));
+            }
         }
-        if (i < n16) emit(__ldcs(qv + i), i);
-        for (int64_t j = (n16 << 4) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
+        for (int64_t j = (n4 << 2) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
     } else {
         for (int64_t j = tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
     }
@@ -1262,8 +1264,9 @@ int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, k
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    // four resident blocks per SM (each builds its own 33 KB table once)
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 32 * 256 - 1) / (32 * 256), 4 * (int64_t)sm_count()));
+    // up to six resident blocks per SM (each builds its own 33 KB table once)
+    const int64_t per_block = 256 * 4 * kDeqBatch;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + per_block - 1) / per_block, 6 * (int64_t)sm_count()));
     dequantize_kernel<<<grid, 256, 0, s>>>(q, n, scale, out);
     return launch_status("dequantize_kernel");
 }
