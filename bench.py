@@ -866,6 +866,16 @@ def run_stack(args, rank, world, local_rank, dev):
     int8_peak = 2.0 * bf16
     gemm_ops = 2.0 * mc * n_loc * STACK_D
     gemm_tops = gemm_ops / (gemm_us / 1e6) / 1e12
+    # the same GEMMs inside the step (per-phase pass: sustained load, power-capped
+    # clocks), against the sustained int8 peak
+    in_step = None
+    if phases and phases.get("gemm"):
+        t_in = phases["gemm"] / (STACK_L * C)
+        a_in = gemm_ops / (t_in / 1e3) / 1e12
+        in_step = {"avg_launch_us": t_in * 1e3, "achieved": a_in, "peak": 2.0 * bf16_sus,
+                   "frac": a_in / (2.0 * bf16_sus),
+                   "peak_source": f"2 x bf16_tflops_sustained ({bf16_sus:.1f}, {peak_src})",
+                   "timing": "CUDA events around each GEMM launch of one eager forward (phases_ms.gemm / launches)"}
     # ours per step: input absmax + quantize, C GEMMs per layer, C quantizes per layer boundary
     launches_per_step = (2 + STACK_L * C + (STACK_L - 1) * C) if pipelined else (1 + 2 * STACK_L - 1)
 
@@ -923,7 +933,8 @@ def run_stack(args, rank, world, local_rank, dev):
                      "algorithmic": f"2*M*N*K = {gemm_ops:.3e} op per launch",
                      "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
                      "timing": f"CUDA events around 4 replays of a graph of the step's {4 * C} GEMM launches "
-                               "(same shapes and weights) alone, right after the timed region"},
+                               "(same shapes and weights) alone, right after the timed region",
+                     "in_step": in_step},
         "phases_ms": phases,
         "output_checksum": checksum,
         "output_checksum_note": "sum of the int32 bit patterns of the full fp32 output over all ranks; equal at "
