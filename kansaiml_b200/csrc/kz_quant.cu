@@ -835,6 +835,17 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
                                                              float* scales_f32, int* status) {
     __shared__ ScaleInfo s_si[kColTile];
     const int64_t n0 = (int64_t)blockIdx.x * kColTile;
+    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    const int64_t n = n0 + 4 * cg;
+    const int64_t k = (int64_t)blockIdx.y * kColRowsPerPass + rg * kColRowsPerThread;
+    const bool active = n < N && k < K;
+    // the tile's loads go out first; the column scales are derived while they are in flight
+    float4 v[kColRowsPerThread];
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < kColRowsPerThread; ++i)
+            v[i] = __ldcs(reinterpret_cast<const float4*>(w + (k + i) * N + n));
+    }
     if (threadIdx.x < kColTile) {
         const int64_t n = n0 + threadIdx.x;
         uint32_t bits = 0;
@@ -854,13 +865,7 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
         }
     }
     __syncthreads();
-    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
-    const int64_t n = n0 + 4 * cg;
-    const int64_t k = (int64_t)blockIdx.y * kColRowsPerPass + rg * kColRowsPerThread;
-    if (n >= N || k >= K) return;
-    float4 v[kColRowsPerThread];
-#pragma unroll
-    for (int i = 0; i < kColRowsPerThread; ++i) v[i] = __ldcs(reinterpret_cast<const float4*>(w + (k + i) * N + n));
+    if (!active) return;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const ScaleInfo si = s_si[4 * cg + j];
@@ -913,10 +918,12 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 
 // -------------------------------------------------------------- dequantize
 
-// Per-tensor dequantize through a lookup table: table[q + 127] =
-// (float)((double)q * scale) holds every value the reference can produce, so
+// Per-tensor dequantize through a lookup table: entry u holds
+// (float)((double)q * scale) for the code q whose byte is u -- every value the
+// reference can produce, indexed by the raw byte so that a lookup costs one
+// byte permute, one address computation and one shared load -- so
 // the per-element work is one shared-memory load (1 B in, 4 B out).  The
-// table is replicated once per bank (entry e of copy b at word e * 32 + b) and
+// table is replicated once per bank (entry u of copy b at word u * 32 + b) and
 // lane b reads copy b, so a warp's 32 lookups never conflict however the codes
 // fall.  Thread t turns one 4-byte word of codes into one 16-byte store, so
 // warps read and write contiguous runs; each thread loads kDeqBatch words
@@ -928,8 +935,8 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
     __shared__ float table[kDeqTable * 32];
     __shared__ float values[kDeqTable];
     if (threadIdx.x < kDeqTable) {
-        const int e = threadIdx.x;   // e = q + 127; e == 255 holds q = -128
-        values[e] = __double2float_rn((double)(e == 255 ? -128 : e - 127) * scale);
+        const int u = threadIdx.x;   // entry u: the code whose two's-complement byte is u
+        values[u] = __double2float_rn((double)(int)(int8_t)(uint8_t)u * scale);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < kDeqTable * 32; i += blockDim.x) table[i] = values[i >> 5];
@@ -937,7 +944,10 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
     const int lane = threadIdx.x & 31;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-    auto lut = [&](uint32_t byte) { return table[(((((int)(int8_t)(uint8_t)byte) + 127) & 255) << 5) + lane]; };
+    const float* tlane = table + lane;
+    // byte k of a word, zero-extended by one byte permute, scaled to its row of the table
+    auto lutw = [&](uint32_t w, int k) { return tlane[__byte_perm(w, 0u, 0x4440u | (uint32_t)k) << 5]; };
+    auto lut = [&](uint32_t byte) { return tlane[(byte & 0xFFu) << 5]; };
     const bool aligned = (reinterpret_cast<uintptr_t>(q) & 3u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
     if (aligned) {
         // thread t converts word t of 4 codes into one 16-byte store, so a
@@ -957,8 +967,7 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
             for (int u = 0; u < kDeqBatch; ++u) {
                 const int64_t i = i0 + u * nthreads;
                 if (i < n4)
-                    __stcs(ov + i, make_float4(lut(w[u] & 0xFF), lut((w[u] >> 8) & 0xFF), lut((w[u] >> 16) & 0xFF),
-                                               lut(w[u] >> 24)));
+                    __stcs(ov + i, make_float4(lutw(w[u], 0), lutw(w[u], 1), lutw(w[u], 2), lutw(w[u], 3)));
             }
         }
         for (int64_t j = (n4 << 2) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
@@ -1169,8 +1178,12 @@ static bool cols_vectorised(const float* w, int64_t K, int64_t N, const int8_t* 
 
 static int64_t col_splits(int64_t K, int64_t N, bool vec) {
     if (vec) {
-        // one 256-row pass per block where that fits in 64 splits
-        int64_t want = (K + kColRowsPerPass - 1) / kColRowsPerPass;
+        // about one resident wave of absmax blocks (three 256-thread blocks per
+        // SM), each looping over its rows: no tail wave
+        const int64_t col_tiles = (N + kColTile - 1) / kColTile;
+        int64_t want = (3 * (int64_t)sm_count()) / col_tiles;
+        const int64_t passes = (K + kColRowsPerPass - 1) / kColRowsPerPass;
+        if (want > passes) want = passes;
         return std::max<int64_t>(1, std::min<int64_t>(want, 64));
     }
     // enough blocks to fill the GPU: ~4 waves of (N / 32) x splits

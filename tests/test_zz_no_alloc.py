@@ -10,8 +10,8 @@ These tests call it through the C ABI and check it against the allocating
 entry point, kz_quantize_cols_f32, and against the oracle's per-column
 quantize, bit for bit (codes and both scale arrays), on calls in a row so a
 stale scratch from an earlier call would show up in a later one: wide and
-narrow weights, shapes whose split count the entry point must cut to fit its
-65536-word scratch, a ragged shape (the unvectorised kernels), and K == 0,
+narrow weights, up to 60000 channels against its 65536-word scratch, a
+ragged shape (the unvectorised kernels), and K == 0,
 where the scratch is cleared instead of written.  This file is collected
 last on purpose; it passes on its own in a fresh process and after the rest
 of the suite.
@@ -53,9 +53,10 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda_device):
     lib = _lib.load()
     stream = torch.cuda.current_stream().cuda_stream
     # in a row: a wide weight with large values; a different shape and
-    # distribution; 8192 and 60000 channels (16 and 2 row splits cut to 8 and
-    # 1 to fit the scratch); a ragged 1000-channel weight; so anything left in
-    # the shared scratch by one call would show in the next
+    # distribution; 8192 and 60000 channels (the row split count times the
+    # channels must fit the 65536-word scratch); a ragged 1000-channel weight
+    # (the unvectorised kernels); so anything left in the shared scratch by
+    # one call would show in the next
     shapes = [((1024, 4096), 3.0, 0), ((4096, 1024), 0.02, 1), ((4096, 8192), 0.5, 2), ((512, 60000), 1.0, 3),
               ((300, 1000), 0.02, 4)]
     for (K, N), std, seed in shapes:
