@@ -45,7 +45,10 @@ constexpr int THREADS = 64 + 32 * EPI_WARPS;
 #ifndef KZ_EPI_DIRECT
 #define KZ_EPI_DIRECT 0   // 1: epilogue stores straight from registers (32-byte stores) instead of TMA
 #endif
-constexpr int GROUP_M = 16;        // tile rasterisation: 16 tile-rows per group
+#ifndef KZ_GROUP_M
+#define KZ_GROUP_M 16   // tile rasterisation: tile-rows per group
+#endif
+constexpr int GROUP_M = KZ_GROUP_M;
 constexpr int EPI_BUF = 32 * 32 * 4;                 // one warp's 32 x 32 fp32/int32 sub-tile
 constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;       // one staging buffer per warp: 32 KB
 constexpr int COLV_BYTES = 2 * BN * 4;               // the tile's column scales and bias (shared by the epilogue)
