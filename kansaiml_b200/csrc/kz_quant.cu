@@ -835,17 +835,6 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
                                                              float* scales_f32, int* status) {
     __shared__ ScaleInfo s_si[kColTile];
     const int64_t n0 = (int64_t)blockIdx.x * kColTile;
-    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
-    const int64_t n = n0 + 4 * cg;
-    const int64_t k = (int64_t)blockIdx.y * kColRowsPerPass + rg * kColRowsPerThread;
-    const bool active = n < N && k < K;
-    // the tile's loads go out first; the column scales are derived while they are in flight
-    float4 v[kColRowsPerThread];
-    if (active) {
-#pragma unroll
-        for (int i = 0; i < kColRowsPerThread; ++i)
-            v[i] = __ldcs(reinterpret_cast<const float4*>(w + (k + i) * N + n));
-    }
     if (threadIdx.x < kColTile) {
         const int64_t n = n0 + threadIdx.x;
         uint32_t bits = 0;
@@ -865,7 +854,13 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
         }
     }
     __syncthreads();
-    if (!active) return;
+    const int cg = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    const int64_t n = n0 + 4 * cg;
+    const int64_t k = (int64_t)blockIdx.y * kColRowsPerPass + rg * kColRowsPerThread;
+    if (n >= N || k >= K) return;
+    float4 v[kColRowsPerThread];
+#pragma unroll
+    for (int i = 0; i < kColRowsPerThread; ++i) v[i] = __ldcs(reinterpret_cast<const float4*>(w + (k + i) * N + n));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const ScaleInfo si = s_si[4 * cg + j];
@@ -1178,12 +1173,8 @@ static bool cols_vectorised(const float* w, int64_t K, int64_t N, const int8_t* 
 
 static int64_t col_splits(int64_t K, int64_t N, bool vec) {
     if (vec) {
-        // about one resident wave of absmax blocks (three 256-thread blocks per
-        // SM), each looping over its rows: no tail wave
-        const int64_t col_tiles = (N + kColTile - 1) / kColTile;
-        int64_t want = (3 * (int64_t)sm_count()) / col_tiles;
-        const int64_t passes = (K + kColRowsPerPass - 1) / kColRowsPerPass;
-        if (want > passes) want = passes;
+        // one 256-row pass per block where that fits in 64 splits
+        int64_t want = (K + kColRowsPerPass - 1) / kColRowsPerPass;
         return std::max<int64_t>(1, std::min<int64_t>(want, 64));
     }
     // enough blocks to fill the GPU: ~4 waves of (N / 32) x splits
