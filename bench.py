@@ -829,6 +829,21 @@ def run_stack(args, rank, world, local_rank, dev):
         dist.all_reduce(chk)
     checksum = f"{int(chk.item()) & 0xFFFFFFFFFFFFFFFF:016x}"
     del y_chk
+    # N > 1: rank 0 also runs the unsharded stack on one GPU over the same
+    # input and weights, and the line records whether the two outputs match
+    parity = None
+    if world > 1:
+        if rank == 0:
+            one = ShardedQLinearStack([weight] * STACK_L, None)
+            g1 = torch.Generator(device=dev)
+            g1.manual_seed(77)
+            x1 = torch.randn((M, STACK_D), generator=g1, device=dev)
+            y1 = one.forward_local(x1, M).data
+            chk1 = int(y1.view(torch.int32).to(torch.int64).sum().item()) & 0xFFFFFFFFFFFFFFFF
+            parity = {"one_gpu_checksum": f"{chk1:016x}", "equal": f"{chk1:016x}" == checksum}
+            del one, x1, y1
+            torch.cuda.empty_cache()
+        dist.barrier()
 
     # per-phase device times of one eager forward (events on the compute stream)
     phases = None
@@ -939,6 +954,7 @@ def run_stack(args, rank, world, local_rank, dev):
         "output_checksum": checksum,
         "output_checksum_note": "sum of the int32 bit patterns of the full fp32 output over all ranks; equal at "
                                 "every N when the sharded forward is bit-identical to the one-GPU forward",
+        "parity_vs_one_gpu": parity,
         "device_status": status,
         "e2e": e2e,
         "cpu_baseline": cpu,
