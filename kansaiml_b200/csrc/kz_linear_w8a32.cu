@@ -90,6 +90,100 @@ __global__ void __launch_bounds__(256) qlinear_w8a32_kernel(const float* __restr
     }
 }
 
+// Large-batch form for aligned shapes (K % 4 == 0, N % 4 == 0, 16-byte
+// aligned x and out, 4-byte aligned q): 128 x 128 tiles, 256 threads, 8 x 8
+// outputs per thread -- rows {4 ty .. +3, 64 + 4 ty .. +3} and the same for
+// columns, so the 16-byte shared loads of a quarter-warp never conflict --
+// giving 128 multiplies and adds per four 16-byte shared loads.  The k tile
+// (8 deep) is double-buffered: the next tile's x (one float4) and codes (one
+// word) are in registers while the current one is consumed.  Same operations
+// in the same k order as the other two kernels.
+constexpr int kTM = 128, kTN = 128, kTK = 8, kTP = kTM + 4;
+
+__global__ void __launch_bounds__(256, 2) qlinear_w8a32_tile128_kernel(const float* __restrict__ x, int64_t M,
+                                                                       int64_t K, const int8_t* __restrict__ q,
+                                                                       double scale, const float* __restrict__ bias,
+                                                                       int64_t N, int act, float* __restrict__ out) {
+    __shared__ float table[256];
+    __shared__ __align__(16) float As[2][kTK][kTP];
+    __shared__ __align__(16) float Bs[2][kTK][kTP];
+    const int tid = threadIdx.x;
+    // entry u: the value of the code whose byte is u (quantize.py:76 + from_flat)
+    table[tid] = __double2float_rn((double)(int)(int8_t)(uint8_t)tid * scale);
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t m0 = blockIdx.y * (int64_t)kTM, n0 = blockIdx.x * (int64_t)kTN;
+    // staging maps: x row xr, k half xh (one float4); code row wk, columns wc .. wc + 3 (one word)
+    const int xr = tid >> 1, xh = tid & 1;
+    const int wk = tid >> 5, wc = (tid & 31) * 4;
+    const bool x_row_ok = m0 + xr < M, w_col_ok = n0 + wc < N;
+    float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t wv = 0;
+    auto fetch = [&](int64_t k0) {
+        const int64_t kx = k0 + 4 * xh, kw = k0 + wk;
+        xv = (x_row_ok && kx < K) ? __ldg(reinterpret_cast<const float4*>(x + (m0 + xr) * K + kx))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv = (w_col_ok && kw < K) ? __ldg(reinterpret_cast<const uint32_t*>(q + kw * N + n0 + wc)) : 0u;
+    };
+    auto stage = [&](int b) {
+        As[b][4 * xh + 0][xr] = xv.x;
+        As[b][4 * xh + 1][xr] = xv.y;
+        As[b][4 * xh + 2][xr] = xv.z;
+        As[b][4 * xh + 3][xr] = xv.w;
+        *reinterpret_cast<float4*>(&Bs[b][wk][wc]) =
+            make_float4(table[wv & 0xFFu], table[(wv >> 8) & 0xFFu], table[(wv >> 16) & 0xFFu], table[wv >> 24]);
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    fetch(0);
+    __syncthreads();   // table ready
+    stage(0);
+    __syncthreads();
+    int buf = 0;
+    for (int64_t k0 = 0; k0 < K; k0 += kTK) {
+        const bool more = k0 + kTK < K;
+        if (more) fetch(k0 + kTK);
+        const int kend = (int)min((int64_t)kTK, K - k0);
+        for (int kk = 0; kk < kend; ++kk) {   // k order preserved
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][4 * ty]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + 4 * ty]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][4 * tx]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + 4 * tx]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+        }
+        if (more) {
+            stage(buf ^ 1);
+            __syncthreads();
+            buf ^= 1;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t m = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + i - 4);
+        if (m >= M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t n = n0 + h * 64 + 4 * tx;
+            if (n >= N) continue;   // N % 4 == 0: the four columns are in or out together
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float t = acc[i][4 * h + j];
+                if (bias) t = __fadd_rn(t, __ldg(bias + n + j));
+                v[j] = act_apply(t, act);
+            }
+            *reinterpret_cast<float4*>(out + m * N + n) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
 // Small-M form: one thread per output, so M x N independent k-ordered chains
 // run at once (the 64 x 64 tiles above give a 64-row batch only N / 64
 // blocks).  A block is 4 rows (one warp each) x 32 columns (one lane each);
@@ -167,8 +261,19 @@ extern "C" int kz_qlinear_w8a32_f32(const float* x, int64_t M, int64_t K, const 
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // Enough 128 x 128 tiles for every SM, aligned shapes: the 8 x 8 per
+    // thread kernel.
+    const int64_t tiles128 = ((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
+    const bool aligned = K % 4 == 0 && N % 4 == 0 && K > 0 &&
+                         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(q) & 3u) == 0;
+    if (aligned && tiles128 >= (int64_t)sm_count() && (M + kTM - 1) / kTM < 65536) {
+        dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+        qlinear_w8a32_tile128_kernel<<<grid, 256, 0, s>>>(x, M, K, q, scale, bias, N, act, out);
+        return launch_status("qlinear_w8a32_tile128_kernel");
+    }
     // Few 64 x 64 tiles (small batches) leave most SMs idle: one thread per
-    // output instead.  Both kernels round identically.
+    // output instead.  All three kernels round identically.
     const int64_t tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
     if (tiles < 2 * (int64_t)sm_count()) {
         KZ_REQUIRE((M + kRowsR - 1) / kRowsR < 65536, "kz_qlinear_w8a32_f32: M too large");

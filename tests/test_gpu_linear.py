@@ -68,11 +68,14 @@ def test_mlp_config1_bit_exact(k):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 33, 10), (3, 784, 65), (64, 784, 256), (64, 256, 10), (300, 200, 300),
-                                   (2048, 512, 1024), (129, 31, 1), (5, 4000, 70), (7, 1537, 40)])
+                                   (2048, 512, 1024), (129, 31, 1), (5, 4000, 70), (7, 1537, 40),
+                                   (1537, 520, 1664), (1024, 2048, 2560), (2000, 517, 2048)])
 def test_w8a32_shapes_vs_oracle(k, M, K, N):
-    """Both W8A32 kernels (one thread per output for small batches, 64 x 64
-    tiles for large ones) against the oracle's k-ordered fp32 loop, bit-exact,
-    on ragged K and N, short and long K."""
+    """The three W8A32 kernels (one thread per output for small batches, 64 x
+    64 tiles, and 128 x 128 tiles with 8 x 8 outputs per thread for large
+    aligned batches -- the last three shapes, one of them with K % 4 != 0,
+    which falls back) against the oracle's k-ordered fp32 loop, bit-exact, on
+    ragged M, K and N, short and long K."""
     kz, nn, kq = k
     rs = np.random.RandomState(M * 7 + K + N)
     x = rs.standard_normal((M, K)).astype(np.float32)
