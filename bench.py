@@ -85,6 +85,15 @@ def parse():
     return ap.parse_args()
 
 
+_T0 = time.time()
+
+
+def _stage(name):
+    """Progress line on stderr (stdout carries only the JSON line)."""
+    print(f"[bench rank {os.environ.get('RANK', '0')} +{time.time() - _T0:7.1f}s] {name}", file=sys.stderr,
+          flush=True)
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -742,6 +751,7 @@ def run_stack(args, rank, world, local_rank, dev):
         g.manual_seed(5000 + l)
         return torch.randn((STACK_D, STACK_D), generator=g, device=dev) * 0.01
 
+    _stage("stack: quantizing weights")
     stack = ShardedQLinearStack([weight] * STACK_L, mesh, exchange=args.exchange)
     M = STACK_M
     g = torch.Generator(device=dev)
@@ -755,18 +765,23 @@ def run_stack(args, rank, world, local_rank, dev):
     C = stack.chunks(M) if pipelined else 1
     if pipelined and world > 1:
         # leave SMs for the NCCL all-gather that overlaps each GEMM chunk
-        _ok(_lib.load().kz_set_sm_count_target(max(2, torch.cuda.get_device_properties(dev).multi_processor_count - 16)))
+        # (KZ_BENCH_SM_TARGET overrides the GEMMs' SM budget; 0 = every SM)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        target = int(os.environ.get("KZ_BENCH_SM_TARGET", max(2, sms - 16)))
+        _ok(_lib.load().kz_set_sm_count_target(target))
 
     def fwd():
         if pipelined:
             return stack.forward_local(x_local, M)
         return stack(x_local)
 
+    _stage("stack: eager warm-up")
     for _ in range(max(args.warmup, 3)):
         fwd()
     torch.cuda.synchronize()
     if device_status() != 0:
         raise RuntimeError("device status set during warm-up")
+    _stage("stack: graph capture")
     graph, graph_note = None, "eager launches"
     if args.graph != "off" and pipelined:
         try:
@@ -797,9 +812,11 @@ def run_stack(args, rank, world, local_rank, dev):
         else:
             fwd()
 
+    _stage(f"stack: warm-up steps ({graph_note})")
     for _ in range(max(args.warmup, 3)):
         step()
     K = args.steps
+    _stage("stack: timed region")
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
@@ -820,6 +837,7 @@ def run_stack(args, rank, world, local_rank, dev):
         ms = float(t.item())
     ms_per_step = ms / K
     status = device_status()
+    _stage("stack: checksum / parity")
     # A checksum of the whole output (the int32 bit patterns of every rank's
     # column shard, summed): sharding changes no arithmetic, so it is the same
     # number at every N when the sharded forward is bit-identical to N = 1.
@@ -845,6 +863,7 @@ def run_stack(args, rank, world, local_rank, dev):
             torch.cuda.empty_cache()
         dist.barrier()
 
+    _stage("stack: per-phase pass")
     # per-phase device times of one eager forward (events on the compute stream)
     phases = None
     if pipelined:
@@ -859,6 +878,7 @@ def run_stack(args, rank, world, local_rank, dev):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             phases = {k: float(v) for k, v in zip(keys, t.tolist())}
 
+    _stage("stack: GEMM alone")
     # the dominant kernel alone: the forward's GEMM launches (same shapes) back to back
     n_loc = STACK_D // world
     mc = M // C
@@ -909,6 +929,7 @@ def run_stack(args, rank, world, local_rank, dev):
     def forward_host_rows(xd):
         return (stack.forward_local(xd, M) if pipelined else stack(xd)).data
 
+    _stage("stack: e2e")
     e2e_ms = _e2e_loop(forward_host_rows, x_host, y_host, x_dev, args.e2e_steps, world, dev)
     e2e = {"value": M / (e2e_ms / args.e2e_steps / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": m_loc * STACK_D * 4 * world, "d2h_bytes_per_step": M * n_loc * 4 * world,
@@ -918,6 +939,7 @@ def run_stack(args, rank, world, local_rank, dev):
 
     kernels = None
     if world == 1 and not args.no_kernels:
+        _stage("kernels")
         kernels = measure_kernels(args, rank, world, local_rank, dev)
     if world > 1:
         del graph
@@ -1158,6 +1180,10 @@ def run_gemm(args, rank, world, local_rank, dev):
 
 def main():
     args = parse()
+    if os.environ.get("KZ_BENCH_TRACEBACK_S"):
+        # diagnosis of a stalled run: every rank prints its threads' stacks periodically
+        import faulthandler
+        faulthandler.dump_traceback_later(int(os.environ["KZ_BENCH_TRACEBACK_S"]), repeat=True)
     if args.impl == "reference":
         run_reference(args)
         return
