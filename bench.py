@@ -794,16 +794,19 @@ def run_stack(args, rank, world, local_rank, dev):
             g_.replay()
             torch.cuda.synchronize()
             graph, graph_note = g_, "one CUDA graph per step (the whole forward, NCCL collectives included)"
+            del g_
         except Exception as e:  # capture unsupported: eager launches
             if args.graph == "on":
                 raise
             graph_note = f"eager launches (graph capture failed: {type(e).__name__})"
+            g_ = None   # release a partial capture (it may hold NCCL work)
             torch.cuda.synchronize()
     # the same decision on every rank
     if world > 1:
         flag = torch.tensor([1 if graph is not None else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if int(flag.item()) == 0 and graph is not None:
+            graph.reset()
             graph, graph_note = None, "eager launches (graph capture failed on another rank)"
 
     def step():
@@ -941,8 +944,12 @@ def run_stack(args, rank, world, local_rank, dev):
     if world == 1 and not args.no_kernels:
         _stage("kernels")
         kernels = measure_kernels(args, rank, world, local_rank, dev)
+    if graph is not None:
+        # a graph holding NCCL collectives must be released before the process
+        # group is destroyed, or the destroy waits for it forever
+        graph.reset()
+        graph = None
     if world > 1:
-        del graph
         stack.close()
         dist.barrier()
         dist.destroy_process_group()
