@@ -21,32 +21,26 @@ Two ways to drive a mesh:
 
 ``ShardedQLinearStack`` is BASELINE config 5: a stack of int8 Linear layers
 whose weights are column-sharded over the mesh (``Shard(1)`` of the reference's
-[in, out] weight), activations quantized per tensor and all-gathered between
-layers.  Per layer: int8 GEMM of the full activation codes against the local
-weight columns (the epilogue also emits absmax partials of its fp32 output) ->
-integer MAX all-reduce of the partials (the global per-tensor absmax) ->
-quantize the local output columns -> all-gather of the int8 codes into the
-rank-major layout [G][M][N/G], which the next GEMM reads directly (a_kblock =
-N/G).  Sharding changes no arithmetic: the result equals the unsharded stack
-bit for bit.
+[in, out] weight), activations row-sharded, quantized per tensor and
+all-gathered between layers.  The default forward (``forward_local``,
+``exchange="collective"``) is pipelined over C row chunks: each rank quantizes
+its own input rows (global absmax by an integer MAX all-reduce), and every
+layer's int8 activations travel as C async NCCL all-gathers while the next
+layer's GEMM runs chunk by chunk, each chunk waiting (a stream dependency, no
+spinning) only for its own all-gather.  Between layers the GEMM epilogues'
+absmax partials are combined and MAX-all-reduced once (the per-tensor scale
+needs the whole layer), each rank quantizes its output columns, and the codes
+land in the rank-major layout [G][M/C][N/G] per chunk, which the next GEMM
+reads directly (a_kblock = N/G).  Sharding changes no arithmetic: the result
+equals the unsharded stack bit for bit.
 
-``exchange="peer"`` (NCCL meshes on GPUs, opt-in) overlaps the all-gather with
-the next GEMM: every rank quantizes its columns straight into block g of a
-buffer the other ranks have mapped (CUDA IPC over NVLink); after a one-word
-barrier the copy engines pull the other ranks' blocks into the local buffer in
-row chunks, publishing a token per chunk, while the next GEMM starts on the
-local block and waits (bounded) on each chunk's token before its first load
-from it.  Measured on B200s it wins at 2 GPUs (4.06 vs 4.12 ms per 4-layer
-forward) and loses at 4 and 8 (2.69 vs 2.57, 3.55 vs 2.52 ms): the copy
-engines move about 470 GB/s per GPU, below NCCL's SM-driven NVLink transfers.
-``exchange="fused"`` moves the all-gather into the GEMM launch itself
-(kz_gemm_i8_allgather): its first CTAs push this rank's block into every other
-rank's buffer over NVLink (stores into peer memory), chunk by chunk, and raise
-the peers' flags, while the other CTAs compute on the chunks already present.
-Bit-exact, but on B200s at 2 GPUs it stays about 5% behind the NCCL
-all-gather plus the plain GEMM: the copy CTAs take SMs from the GEMM and their
-traffic slows the computing CTAs even when nothing waits.  The default is
-``exchange="collective"``, the NCCL all-gather.
+Two earlier exchanges stay as options: ``exchange="peer"`` (IPC-exported
+gather buffers pulled by the copy engines in row chunks while the gated GEMM
+waits, bounded, on each chunk's token) and ``exchange="fused"`` (the
+all-gather inside the GEMM launch: its first CTAs push this rank's block to
+every peer with 16-byte stores and raise the peers' flags).  Both are
+bit-exact; on B200s they lost to NCCL past two GPUs (one copy-engine stream
+moved ~470 GB/s per GPU; the copy CTAs slowed the computing ones).
 """
 import ctypes
 from concurrent.futures import ThreadPoolExecutor, wait
