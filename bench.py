@@ -74,9 +74,10 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay the stack's forward from a CUDA graph (auto: when capture succeeds)")
-    ap.add_argument("--exchange", choices=["peer", "collective", "fused"], default=None,
-                    help="stack: pipelined NCCL all-gathers (collective, default), copy-engine pulls feeding the "
-                         "gated GEMM (peer) or the all-gather inside the GEMM launch (fused)")
+    ap.add_argument("--exchange", choices=["peer", "collective", "fused", "ce"], default=None,
+                    help="stack: pipelined NCCL all-gathers (collective, default), pipelined copy-engine pulls "
+                         "(ce), copy-engine pulls feeding the gated GEMM (peer) or the all-gather inside the GEMM "
+                         "launch (fused)")
     ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp", "kernels", "gemm"],
                     default="stack",
                     help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
@@ -757,7 +758,7 @@ def run_stack(args, rank, world, local_rank, dev):
     g = torch.Generator(device=dev)
     g.manual_seed(77)
     x_full = torch.randn((M, STACK_D), generator=g, device=dev)
-    pipelined = stack.exchange == "collective"
+    pipelined = stack.exchange in ("collective", "ce")
     x_local = stack.local_input(x_full) if (pipelined and world > 1) else x_full
     if pipelined:
         del x_full

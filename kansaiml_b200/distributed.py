@@ -497,6 +497,79 @@ def pipeline_input_rows(M, world, rank):
     return [(c * mc + rank * mp, c * mc + (rank + 1) * mp) for c in range(C)]
 
 
+class _CopyEngineGather:
+    """Two gather buffers per rank (one per exchange parity), exported to the
+    other ranks through CUDA IPC, each holding C x G blocks: block (c, g) is
+    rank g's share of row chunk c.  A rank writes its own blocks (its quantize
+    writes there directly); ``pull`` copies every other rank's blocks into the
+    local buffer with the copy engines -- one stream per peer, so the peers'
+    copies run side by side, chunk 0 first -- and returns, per chunk, the
+    events its copies complete, for the GEMM of that chunk to wait on.  The
+    copy engines use no SM, so the GEMM of chunk c runs on every SM it asked
+    for while chunk c + 1 arrives."""
+
+    def __init__(self, nbytes, world, rank, group, device):
+        self.lib = _lib.load()
+        self.world, self.rank, self.group, self.device = world, rank, group, device
+        self.own, handles = [], []
+        for _ in range(2):
+            p, h = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.KZ_IPC_HANDLE_BYTES)
+            _lib.check(self.lib.kz_peer_alloc(nbytes, ctypes.byref(p), h), "kz_peer_alloc")
+            self.own.append(p.value)
+            handles.append(h.raw)
+        self.nbytes = nbytes
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handles, group=group)
+        self.peer = {}
+        for r in range(world):
+            if r != rank:
+                ptrs = []
+                for i in range(2):
+                    p = ctypes.c_void_p()
+                    _lib.check(self.lib.kz_peer_open(gathered[r][i], ctypes.byref(p)), "kz_peer_open")
+                    ptrs.append(p.value)
+                self.peer[r] = ptrs
+        self.streams = {r: torch.cuda.Stream(device) for r in self.peer}
+        # kz_copy_and_flag also writes a token; these words take it (nothing reads them)
+        self.sink = torch.zeros(world, dtype=torch.int32, device=device)
+        self.one = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def block(self, parity, c, g, blk):
+        return self.own[parity] + (c * self.world + g) * blk
+
+    def pull(self, parity, chunks, blk):
+        """Once every rank's own blocks of `parity` are written (an NCCL
+        one-word barrier), copy the peers' blocks in; returns [events of
+        chunk c for c in range(chunks)]."""
+        cur = torch.cuda.current_stream(self.device)
+        dist.all_reduce(self.one, group=self.group)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        events = [[] for _ in range(chunks)]
+        for h, st in self.streams.items():
+            st.wait_event(ready)
+            for c in range(chunks):
+                off = (c * self.world + h) * blk
+                _lib.check(self.lib.kz_copy_and_flag(self.own[parity] + off, self.peer[h][parity] + off, blk,
+                                                     self.sink.data_ptr() + 4 * h, 1, st.cuda_stream),
+                           "kz_copy_and_flag")
+                e = torch.cuda.Event()
+                e.record(st)
+                events[c].append(e)
+        return events
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for ptrs in self.peer.values():
+            for p in ptrs:
+                _lib.check(self.lib.kz_peer_close(ctypes.c_void_p(p)), "kz_peer_close")
+        dist.barrier(group=self.group)
+        for p in self.own:
+            _lib.check(self.lib.kz_peer_free(ctypes.c_void_p(p)), "kz_peer_free")
+        self.own, self.peer = [], {}
+
+
 class _PhaseEvents:
     """CUDA events around the phases of a forward on the current stream
     (only when enabled).  ``finish()`` synchronises and returns
@@ -568,7 +641,7 @@ class ShardedQLinearStack:
         self.partials = None
         if exchange is None:
             exchange = "collective"
-        if exchange not in ("peer", "collective", "fused"):
+        if exchange not in ("peer", "collective", "fused", "ce"):
             raise ValueError(f"unknown exchange {exchange!r}")
         if exchange != "collective" and self.world > 1 and dist.get_backend(self.group) != "nccl":
             raise ValueError(f'exchange="{exchange}" needs an NCCL mesh on GPUs')
@@ -576,6 +649,7 @@ class ShardedQLinearStack:
         self.copy_ctas = 8
         self._peer = None
         self._bufs = {}
+        self._ce = None
         self.timing = False        # record per-phase CUDA-event times in forward_local (phase_times)
         self._phases = None
 
@@ -584,6 +658,9 @@ class ShardedQLinearStack:
         if self._peer is not None:
             self._peer.close()
             self._peer = None
+        if self._ce is not None:
+            self._ce.close()
+            self._ce = None
 
     # ------------------------------------------------- pipelined forward
 
@@ -626,6 +703,8 @@ class ShardedQLinearStack:
         mp = mc // G
         if xd.shape[0] != C * mp:
             raise ValueError(f"local input has {xd.shape[0]} rows, expected {C * mp}")
+        if self.exchange == "ce" and G > 1:
+            return self._forward_local_ce(xd.contiguous(), M)
         ev = _PhaseEvents(self.timing, dev)
         # layer-0 input: absmax of the local rows -> global absmax -> local codes
         ev.begin("input_quantize")
@@ -688,6 +767,79 @@ class ShardedQLinearStack:
         (synchronises the device), else None."""
         return self._phases.finish() if self._phases is not None else None
 
+    def _forward_local_ce(self, xd, M):
+        """forward_local with the copy-engine exchange (exchange="ce"): the
+        same chunking, row ownership, scales and layouts, but each rank
+        quantizes straight into its blocks of an IPC-exported gather buffer
+        and the other ranks' blocks arrive by copy-engine pulls
+        (_CopyEngineGather) instead of NCCL all-gathers; NCCL carries only the
+        absmax all-reduces and a one-word barrier per exchange.  The absmax
+        all-reduce of each exchange is also what keeps a buffer from being
+        rewritten while a peer still reads it: every rank passes it only after
+        its GEMMs of the previous layer, which waited for their pulls."""
+        dev = xd.device
+        G, C = self.world, self.chunks(M)
+        mc, mp = M // C, M // (C * self.world)
+        blks = [mp * self.layers[0][1]] + [mc * qt.shape[1] for qt, _, _ in self.layers[:-1]]
+        need = C * G * max(blks)
+        if self._ce is None or self._ce.nbytes < need:
+            self.close()
+            self._ce = _CopyEngineGather(need, G, self.rank, self.group, dev)
+        ce = self._ce
+        sh = stream_handle(dev)
+        cur = torch.cuda.current_stream(dev)
+        ev = _PhaseEvents(self.timing, dev)
+        # layer-0 input: global absmax, then this rank's rows straight into its blocks
+        ev.begin("input_quantize")
+        parts = self._zeroed("in_parts", (_lib.KZ_PARTIALS_WORDS,), torch.int32, dev)
+        absmax_partials_device(xd, parts)
+        allreduce_partials_max(parts, self.group)
+        s64 = torch.empty(1, dtype=torch.float64, device=dev)
+        a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
+        K0 = self.layers[0][1]
+        blk, parity = blks[0], 0
+        for c in range(C):
+            _lib.call("kz_quantize_partials_f32", ptr(xd[c * mp:(c + 1) * mp]), mp * K0, ptr(parts),
+                      ce.block(parity, c, self.rank, blk), ptr(s64), ptr(a_s32), sh)
+        events = ce.pull(parity, C, blk)
+        ev.end()
+        a_kblock = K0
+        y = None
+        for li, (qt, K, N) in enumerate(self.layers):
+            n_loc = qt.shape[1]
+            last = li == len(self.layers) - 1
+            y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
+            pb = None if last else self._zeroed(("chunk_parts", C), (C, _lib.KZ_PARTIALS_WORDS), torch.int32, dev)
+            for c in range(C):
+                ev.begin("wait_allgather")
+                for e in events[c]:
+                    cur.wait_event(e)
+                ev.end()
+                ev.begin("gemm")
+                _lib.call("kz_gemm_i8", ce.own[parity] + c * G * blk, ptr(qt.kmajor()), mc, n_loc, K, a_kblock,
+                          ptr(a_s32), 0, ptr(qt.scale_f32), 1, None, _lib.KZ_ACT_NONE, ptr(y[c * mc:(c + 1) * mc]),
+                          None, n_loc, None if last else ptr(pb[c]), sh)
+                ev.end()
+            if last:
+                break
+            ev.begin("allreduce_max")
+            lp = torch.amax(pb, 0) if C > 1 else pb[0]
+            allreduce_partials_max(lp, self.group)
+            ev.end()
+            ev.begin("quantize")
+            parity ^= 1
+            blk = blks[li + 1]
+            s64 = torch.empty(1, dtype=torch.float64, device=dev)
+            a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
+            for c in range(C):
+                _lib.call("kz_quantize_partials_f32", ptr(y[c * mc:(c + 1) * mc]), mc * n_loc, ptr(lp),
+                          ce.block(parity, c, self.rank, blk), ptr(s64), ptr(a_s32), sh)
+            events = ce.pull(parity, C, blk)
+            ev.end()
+            a_kblock = n_loc
+        self._phases = ev
+        return Tensor(y)
+
     def forward(self, x, return_local=True):
         """x: fp32 [M, K] replicated on every rank.  Returns the last layer's
         fp32 output: this rank's column shard (return_local) or the full
@@ -696,7 +848,7 @@ class ShardedQLinearStack:
         own rows of x (forward_local); otherwise every rank quantizes all of x."""
         xd = as_tensor(x).data.contiguous()
         M = xd.shape[0]
-        if self.exchange == "collective" and self.chunks(M) > 0:
+        if self.exchange in ("collective", "ce") and self.chunks(M) > 0:
             y = self.forward_local(self.local_input(xd) if self.world > 1 else xd, M).data
         else:
             y = self._forward_replicated(xd)

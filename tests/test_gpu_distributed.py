@@ -87,7 +87,7 @@ def _spmd_worker(rank, world, port, q, exchange):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange", ["collective", "peer", "fused"])
+@pytest.mark.parametrize("exchange", ["collective", "peer", "fused", "ce"])
 def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
     """Two ranks over NCCL: the plain all-gather; the all-gather overlapped
     with the next GEMM (peer buffers + copy engines + the gated GEMM); and the
@@ -113,7 +113,7 @@ def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
 M_PIPE = 2048   # four row chunks of 512 on two ranks
 
 
-def _pipelined_worker(rank, world, port, q):
+def _pipelined_worker(rank, world, port, q, exchange="collective"):
     try:
         import datetime
         import torch.distributed as dist
@@ -124,7 +124,7 @@ def _pipelined_worker(rank, world, port, q):
         from kansaiml_b200 import _lib
         from kansaiml_b200 import distributed as kd
         mesh = kd.DeviceMesh.spmd()
-        stack = kd.ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh)
+        stack = kd.ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh, exchange=exchange)
         assert stack.chunks(M_PIPE) == 4
         x = torch.from_numpy(make_x(M_PIPE)).cuda()
         full = stack(x, return_local=False).numpy()
@@ -159,7 +159,9 @@ def _pipelined_worker(rank, world, port, q):
         ok = ok and sh.shape == [3 * world, 2]
         from kansaiml_b200.quantize import device_status
         assert device_status() == 0
+        g.reset()
         del g
+        stack.close()
         q.put((rank, full if ok else "graph replay, phases or dtensor_grad differ"))
         dist.barrier()
         dist.destroy_process_group()
@@ -173,18 +175,20 @@ def kz_tensor(t):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_stack_pipelined_two_gpus_graph_and_grad():
+@pytest.mark.parametrize("exchange", ["collective", "ce"])
+def test_stack_pipelined_two_gpus_graph_and_grad(exchange):
     """Two ranks, 2048 rows in four row chunks: the pipelined forward (input
-    rows quantized per rank and all-gathered chunk by chunk, every layer's
-    codes all-gathered chunk by chunk under the next GEMM) equals the oracle's
-    unsharded chain bit for bit, also when replayed from a CUDA graph that
-    captured its NCCL collectives; dtensor_grad's NCCL reductions match the
+    rows quantized per rank and exchanged chunk by chunk, every layer's codes
+    exchanged chunk by chunk under the next GEMM -- by NCCL all-gathers, or by
+    copy-engine pulls from IPC-shared buffers) equals the oracle's unsharded
+    chain bit for bit, also when replayed from a CUDA graph that captured its
+    collectives and copies; dtensor_grad's NCCL reductions match the
     reference's double-precision sum."""
     expected_pipe = oracle_chain(make_x(M_PIPE), make_weights())
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_pipelined_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_pipelined_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
