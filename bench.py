@@ -83,6 +83,8 @@ def parse():
                     help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
                          "mlp: config 1; kernels: the per-kernel entries alone; gemm: one GEMM shape (--shape)")
     ap.add_argument("--shape", default="8192,16384,16384", help="gemm workload: M,N,K")
+    ap.add_argument("--tp", type=int, default=None,
+                    help="stack: column-sharding group size (default: the stack's, N up to 4, else 4)")
     return ap.parse_args()
 
 
@@ -753,7 +755,7 @@ def run_stack(args, rank, world, local_rank, dev):
         return torch.randn((STACK_D, STACK_D), generator=g, device=dev) * 0.01
 
     _stage("stack: quantizing weights")
-    stack = ShardedQLinearStack([weight] * STACK_L, mesh, exchange=args.exchange)
+    stack = ShardedQLinearStack([weight] * STACK_L, mesh, exchange=args.exchange, tp=args.tp)
     M = STACK_M
     g = torch.Generator(device=dev)
     g.manual_seed(77)
@@ -884,8 +886,8 @@ def run_stack(args, rank, world, local_rank, dev):
 
     _stage("stack: GEMM alone")
     # the dominant kernel alone: the forward's GEMM launches (same shapes) back to back
-    n_loc = STACK_D // world
-    mc = M // C
+    n_loc = STACK_D // stack.tp
+    mc = (M // stack.dp) // C
     qt0 = stack.layers[0][0]
     a_chunk = torch.randint(-127, 128, (mc, STACK_D), dtype=torch.int8, device=dev)
     ys = [torch.empty((mc, n_loc), dtype=torch.float32, device=dev) for _ in range(2)]
@@ -925,7 +927,7 @@ def run_stack(args, rank, world, local_rank, dev):
     rs = np.random.RandomState(2000 + rank)
     x_host = [torch.from_numpy(rs.standard_normal((m_loc, STACK_D)).astype(np.float32)).pin_memory()
               for _ in range(NB)]
-    y_host = [torch.empty((M, n_loc), dtype=torch.float32).pin_memory() for _ in range(NB)]
+    y_host = [torch.empty((M // stack.dp, n_loc), dtype=torch.float32).pin_memory() for _ in range(NB)]
     x_dev = [torch.empty((m_loc, STACK_D), dtype=torch.float32, device=dev) for _ in range(NB)]
     del x_local
     torch.cuda.empty_cache()
@@ -936,7 +938,8 @@ def run_stack(args, rank, world, local_rank, dev):
     _stage("stack: e2e")
     e2e_ms = _e2e_loop(forward_host_rows, x_host, y_host, x_dev, args.e2e_steps, world, dev)
     e2e = {"value": M / (e2e_ms / args.e2e_steps / 1e3), "unit": "tokens/s",
-           "h2d_bytes_per_step": m_loc * STACK_D * 4 * world, "d2h_bytes_per_step": M * n_loc * 4 * world,
+           "h2d_bytes_per_step": m_loc * STACK_D * 4 * world,
+           "d2h_bytes_per_step": (M // stack.dp) * n_loc * 4 * world,
            "note": "bytes summed over ranks: each rank uploads its input rows and downloads its output columns"}
     del x_host, y_host, x_dev
     torch.cuda.empty_cache()
@@ -965,14 +968,15 @@ def run_stack(args, rank, world, local_rank, dev):
         "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": STACK_WORKLOAD, "global_batch": M, "seq_len": None,
-                   "parallelism": f"tp{world} (weights column-sharded, activations row-sharded)",
+                   "parallelism": (f"dp{stack.dp} x tp{stack.tp} (weights column-sharded within groups of "
+                                   f"{stack.tp}, activations row-sharded across them)"),
                    "exchange": stack.exchange, "row_chunks": C, "launch": graph_note,
                    "l2": "inputs larger than L2 (weights 1 GiB int8 codes in total, input 512 MiB fp32)"},
         "tops": ops / (ms_per_step / 1e3) / 1e12,
         "gpu_launches": launches_per_step * K,
         "roofline": {"kernel": "gemm_i8_kernel", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                      "unit": "TOP/s", "frac": gemm_tops / int8_peak,
-                     "traffic": profile_traffic(f"gemm_i8_config5_tp{world}"),
+                     "traffic": profile_traffic(f"gemm_i8_{mc}x{n_loc}x{STACK_D}"),
                      "avg_launch_us": gemm_us,
                      "shape": f"M={mc} N={n_loc} K={STACK_D} (one row chunk of one layer on one rank)",
                      "algorithmic": f"2*M*N*K = {gemm_ops:.3e} op per launch",

@@ -610,20 +610,44 @@ class ShardedQLinearStack:
     weights: list of fp32 [K, N] tensors (the reference layout), or callables
     ``w(l)`` returning layer l's full weight on the current device.  Each rank
     keeps only its columns, quantized per output channel.  N / G must be a
-    multiple of 128 between layers (the GEMM's K block)."""
+    multiple of 128 between layers (the GEMM's K block).
 
-    def __init__(self, weights, mesh=None, exchange=None):
+    tp: the size of the column-sharding groups.  With tp = the mesh size (the
+    default up to 4 ranks) every rank holds 1/tp of every weight and all
+    ranks share the batch's rows; with tp < mesh size (the default at 8
+    ranks: two groups of 4) consecutive groups of tp ranks each take
+    1/(mesh size / tp) of the batch's rows -- the activations row-sharded
+    across groups, the weights column-sharded within one -- so each rank
+    exchanges 1/(mesh size / tp) as many activation bytes for the same GEMM
+    work.  The per-tensor absmax is still all-reduced over every rank, so the
+    output equals the unsharded stack's bit for bit either way."""
+
+    def __init__(self, weights, mesh=None, exchange=None, tp=None):
         self.mesh = mesh
         self.world = len(mesh) if mesh is not None and mesh.is_spmd else 1
         self.rank = mesh.rank if mesh is not None and mesh.is_spmd else 0
         self.group = mesh.group if mesh is not None and mesh.is_spmd else None
+        if tp is None:
+            tp = 4 if self.world > 4 and self.world % 4 == 0 else self.world
+        if tp < 1 or self.world % tp:
+            raise ValueError(f"tp={tp} must divide the mesh size {self.world}")
+        if tp < self.world and self.group is not None:
+            raise ValueError("tp < mesh size needs the default process group")
+        self.tp, self.dp = tp, self.world // tp
+        self.g, self.d = self.rank % tp, self.rank // tp      # column shard, row group
+        self.xgroup = self.group                              # the exchange group: this rank's tp ranks
+        if tp < self.world:
+            for d in range(self.dp):                          # every rank creates every group, in order
+                grp = dist.new_group(list(range(d * tp, (d + 1) * tp)))
+                if d == self.d:
+                    self.xgroup = grp
         self.layers = []
         for i, w in enumerate(weights):
             full = w(i) if callable(w) else as_tensor(w).data
             K, N = full.shape
-            if N % self.world:
-                raise ValueError(f"layer {i}: out_features {N} is not divisible by the mesh size {self.world}")
-            lo, hi = column_shard_bounds(N, self.rank, self.world)
+            if N % self.tp:
+                raise ValueError(f"layer {i}: out_features {N} is not divisible by the group size {self.tp}")
+            lo, hi = column_shard_bounds(N, self.g, self.tp)
             shard = full[:, lo:hi].contiguous()
             del full
             qT, s64, s32 = quantize_cols_device(shard)
@@ -634,18 +658,23 @@ class ShardedQLinearStack:
         for i in range(1, len(self.layers)):
             if self.layers[i][1] != self.layers[i - 1][2]:
                 raise ValueError("consecutive layers' shapes do not chain")
-        if self.world > 1:
-            n_loc = self.layers[0][2] // self.world
+        if self.tp > 1:
+            n_loc = self.layers[0][2] // self.tp
             if n_loc % 128:
-                raise ValueError("out_features / mesh size must be a multiple of 128")
+                raise ValueError("out_features / group size must be a multiple of 128")
         self.partials = None
         if exchange is None:
-            exchange = "collective"
+            # the copy-engine exchange where it can run (GPUs on NCCL): it beat
+            # the NCCL all-gathers at 2 and 4 ranks per column-sharding group
+            nccl = self.world > 1 and dist.get_backend(self.group) == "nccl"
+            exchange = "ce" if nccl and self.tp > 1 else "collective"
         if exchange not in ("peer", "collective", "fused", "ce"):
             raise ValueError(f"unknown exchange {exchange!r}")
         if exchange != "collective" and self.world > 1 and dist.get_backend(self.group) != "nccl":
             raise ValueError(f'exchange="{exchange}" needs an NCCL mesh on GPUs')
-        self.exchange = exchange if self.world > 1 else "collective"
+        if tp < self.world and exchange not in ("collective", "ce"):
+            raise ValueError(f'exchange="{exchange}" shards columns over the whole mesh (tp = mesh size)')
+        self.exchange = exchange if self.tp > 1 else "collective"
         self.copy_ctas = 8
         self._peer = None
         self._bufs = {}
@@ -665,12 +694,20 @@ class ShardedQLinearStack:
     # ------------------------------------------------- pipelined forward
 
     def chunks(self, M):
-        """Row chunks of the pipelined exchange (pipeline_chunks)."""
-        return pipeline_chunks(M, self.world)
+        """Row chunks of the pipelined exchange (pipeline_chunks of this row
+        group's M / dp rows over tp ranks); 0 when M does not split."""
+        if M % self.dp:
+            return 0
+        return pipeline_chunks(M // self.dp, self.tp)
 
     def input_rows(self, M):
-        """This rank's rows of an [M, K] input in the pipelined layout (pipeline_input_rows)."""
-        return pipeline_input_rows(M, self.world, self.rank)
+        """This rank's rows of an [M, K] input in the pipelined layout: the
+        pipeline_input_rows of its column-shard index within its row group's
+        M / dp rows."""
+        if self.chunks(M) == 0:
+            raise ValueError(f"{M} rows do not split into equal blocks over {self.world} ranks")
+        base = self.d * (M // self.dp)
+        return [(base + a, base + b) for a, b in pipeline_input_rows(M // self.dp, self.tp, self.g)]
 
     def local_input(self, x):
         """This rank's rows (input_rows) of a replicated [M, K] input, stacked."""
@@ -686,8 +723,8 @@ class ShardedQLinearStack:
 
     def forward_local(self, x_local, M):
         """The stack on this rank's input rows (local_input / input_rows
-        layout, fp32 [M / world, K]).  Returns this rank's fp32 column shard
-        of the last layer's output, [M, N / world].
+        layout, fp32 [M / world, K]).  Returns this rank's block of the last
+        layer's fp32 output: its row group's M / dp rows x its N / tp columns.
 
         Pipelined over C row chunks: each layer's int8 activations travel as
         C NCCL all-gathers (async, on the process group's stream), and the
@@ -698,7 +735,8 @@ class ShardedQLinearStack:
         partials per chunk, combined and MAX-all-reduced once per layer."""
         xd = as_tensor(x_local).data
         dev = xd.device
-        G, C = self.world, self.chunks(M)
+        G, C = self.tp, self.chunks(M)
+        M = M // self.dp              # this row group's rows
         mc = M // C
         mp = mc // G
         if xd.shape[0] != C * mp:
@@ -710,7 +748,7 @@ class ShardedQLinearStack:
         ev.begin("input_quantize")
         parts = self._zeroed("in_parts", (_lib.KZ_PARTIALS_WORDS,), torch.int32, dev)
         absmax_partials_device(xd, parts)
-        if G > 1:
+        if self.world > 1:
             allreduce_partials_max(parts, self.group)
         codes, _, a_s32 = quantize_partials_device(xd, parts)
         ev.end()
@@ -720,7 +758,7 @@ class ShardedQLinearStack:
             A = torch.empty((M, K0), dtype=torch.int8, device=dev)
             for c in range(C):
                 works[c] = _all_gather_async(A[c * mc:(c + 1) * mc].view(G, mp, K0), codes[c * mp:(c + 1) * mp],
-                                             self.group)
+                                             self.xgroup)
         else:
             A = codes
         a_chunks = [(A[c * mc:(c + 1) * mc], K0) for c in range(C)]
@@ -744,7 +782,7 @@ class ShardedQLinearStack:
                 break
             ev.begin("allreduce_max")
             lp = torch.amax(pb, 0) if C > 1 else pb[0]
-            if G > 1:
+            if self.world > 1:
                 allreduce_partials_max(lp, self.group)
             ev.end()
             ev.begin("quantize")
@@ -756,7 +794,7 @@ class ShardedQLinearStack:
                 rows = slice(c * mc, (c + 1) * mc)
                 quantize_partials_device(y[rows], lp, q=yq[rows], s64=s64, s32=a_s32)
                 if G > 1:
-                    works[c] = _all_gather_async(gathered[c], yq[rows], self.group)
+                    works[c] = _all_gather_async(gathered[c], yq[rows], self.xgroup)
             ev.end()
             a_chunks = [(gathered[c], n_loc) for c in range(C)] if G > 1 else [(yq, N)]
         self._phases = ev
@@ -778,13 +816,13 @@ class ShardedQLinearStack:
         rewritten while a peer still reads it: every rank passes it only after
         its GEMMs of the previous layer, which waited for their pulls."""
         dev = xd.device
-        G, C = self.world, self.chunks(M)
-        mc, mp = M // C, M // (C * self.world)
+        G, C = self.tp, pipeline_chunks(M, self.tp)     # M: this row group's rows
+        mc, mp = M // C, M // (C * G)
         blks = [mp * self.layers[0][1]] + [mc * qt.shape[1] for qt, _, _ in self.layers[:-1]]
         need = C * G * max(blks)
         if self._ce is None or self._ce.nbytes < need:
             self.close()
-            self._ce = _CopyEngineGather(need, G, self.rank, self.group, dev)
+            self._ce = _CopyEngineGather(need, G, self.g, self.xgroup, dev)
         ce = self._ce
         sh = stream_handle(dev)
         cur = torch.cuda.current_stream(dev)
@@ -800,7 +838,7 @@ class ShardedQLinearStack:
         blk, parity = blks[0], 0
         for c in range(C):
             _lib.call("kz_quantize_partials_f32", ptr(xd[c * mp:(c + 1) * mp]), mp * K0, ptr(parts),
-                      ce.block(parity, c, self.rank, blk), ptr(s64), ptr(a_s32), sh)
+                      ce.block(parity, c, self.g, blk), ptr(s64), ptr(a_s32), sh)
         events = ce.pull(parity, C, blk)
         ev.end()
         a_kblock = K0
@@ -833,7 +871,7 @@ class ShardedQLinearStack:
             a_s32 = torch.empty(1, dtype=torch.float32, device=dev)
             for c in range(C):
                 _lib.call("kz_quantize_partials_f32", ptr(y[c * mc:(c + 1) * mc]), mc * n_loc, ptr(lp),
-                          ce.block(parity, c, self.rank, blk), ptr(s64), ptr(a_s32), sh)
+                          ce.block(parity, c, self.g, blk), ptr(s64), ptr(a_s32), sh)
             events = ce.pull(parity, C, blk)
             ev.end()
             a_kblock = n_loc
@@ -850,12 +888,15 @@ class ShardedQLinearStack:
         M = xd.shape[0]
         if self.exchange in ("collective", "ce") and self.chunks(M) > 0:
             y = self.forward_local(self.local_input(xd) if self.world > 1 else xd, M).data
+        elif self.tp < self.world:
+            raise ValueError(f"{M} rows do not split into {self.dp} row groups of equal pipelined blocks")
         else:
             y = self._forward_replicated(xd)
         if return_local or self.world == 1:
             return Tensor(y)
-        parts = allgather_blocked(y, self.group)        # [G, M, n_loc] fp32
-        return Tensor(parts.permute(1, 0, 2).reshape(M, -1))
+        parts = allgather_blocked(y.contiguous(), self.group)     # [world, M / dp, N / tp], rank = d * tp + g
+        n_loc = parts.shape[2]
+        return Tensor(parts.view(self.dp, self.tp, M // self.dp, n_loc).permute(0, 2, 1, 3).reshape(M, -1))
 
     def _forward_replicated(self, xd):
         """Every rank quantizes the whole replicated input; one all-gather per

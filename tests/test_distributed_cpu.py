@@ -398,3 +398,51 @@ def test_pipelined_stack_world2_gloo_matches_oracle_chain():
     for r in range(2):
         assert isinstance(res[r], np.ndarray), res[r]
         assert res[r].tobytes() == want.tobytes()
+
+
+def _pipe2d_worker(rank, world, port, q, tp):
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        _install_cpu_kernels()
+        stack = kd.ShardedQLinearStack([torch.from_numpy(w) for w in _pipe_weights()], kd.DeviceMesh.spmd(), tp=tp)
+        assert (stack.tp, stack.dp, stack.g, stack.d) == (tp, world // tp, rank % tp, rank // tp)
+        rows = stack.input_rows(PIPE_M)
+        y = stack(torch.from_numpy(_pipe_x()), return_local=False).numpy()
+        q.put((rank, (y, rows)))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+def test_pipelined_stack_row_groups_world4_gloo_matches_oracle_chain():
+    """Four gloo ranks as two row groups of two column shards (tp=2): each
+    group runs the pipelined forward on half the rows, the absmax is
+    all-reduced over all four ranks, and the gathered output equals the
+    oracle's unsharded chain; the four ranks' input rows tile the batch."""
+    from oracle import cpu as ocpu
+    a, s_a = ocpu.quantize_tensor(_pipe_x())
+    want = None
+    for i, w in enumerate(_pipe_weights()):
+        wq, ws = ocpu.quantize_cols(w)
+        want = ocpu.epilogue(ocpu.gemm_i8(a, wq), s_a, ws)
+        if i < len(PIPE_DIMS) - 2:
+            a, s_a = ocpu.quantize_tensor(want)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pipe2d_worker, args=(r, 4, port, q, 2)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(4):
+        r, v = q.get(timeout=300)
+        res[r] = v
+    for p in procs:
+        p.join(timeout=60)
+    covered = []
+    for r in range(4):
+        assert isinstance(res[r], tuple), res[r]
+        y, rows = res[r]
+        assert y.tobytes() == want.tobytes()
+        covered += [i for a0, b0 in rows for i in range(a0, b0)]
+    assert sorted(covered) == list(range(PIPE_M))
