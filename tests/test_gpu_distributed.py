@@ -61,7 +61,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _spmd_worker(rank, world, port, q, exchange):
+def _spmd_worker(rank, world, port, q, exchange, tp=None):
     try:
         import datetime
         import torch.distributed as dist
@@ -71,8 +71,9 @@ def _spmd_worker(rank, world, port, q, exchange):
                                 timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
         from kansaiml_b200.distributed import DeviceMesh, ShardedQLinearStack
         mesh = DeviceMesh.spmd()
-        stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh, exchange=exchange)
-        assert stack.exchange == exchange
+        stack = ShardedQLinearStack([torch.from_numpy(w).cuda() for w in make_weights()], mesh, exchange=exchange,
+                                    tp=tp)
+        assert stack.exchange == (exchange if stack.tp > 1 else "collective")
         x = torch.from_numpy(make_x()).cuda()
         y = stack(x, return_local=False).numpy()
         y2 = stack(x, return_local=False).numpy()   # buffers, flags and tokens reused
@@ -106,6 +107,31 @@ def test_stack_two_gpus_spmd_bit_exact(expected, exchange):
     for p in procs:
         p.join(timeout=120)
     for r in range(2):
+        assert isinstance(res[r], np.ndarray), res[r]
+        assert res[r].tobytes() == expected.tobytes()
+
+
+@pytest.mark.parametrize("world,tp,exchange", [(2, 1, "collective"), (4, 2, "ce"), (4, 2, "collective")])
+def test_stack_row_groups_spmd_bit_exact(expected, world, tp, exchange):
+    """Row groups x column shards: world / tp groups of tp ranks, each group
+    on its own rows (tp = 1 is pure data parallelism), the absmax all-reduced
+    over every rank: the gathered output equals the oracle's unsharded chain
+    bit for bit.  Needs `world` GPUs."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_spmd_worker, args=(r, world, port, q, exchange, tp)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, y = q.get(timeout=300)
+        res[r] = y
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
         assert isinstance(res[r], np.ndarray), res[r]
         assert res[r].tobytes() == expected.tobytes()
 
