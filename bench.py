@@ -4,18 +4,19 @@
 
 Default workload ("config 5", the north star's
 sharded matmul): a stack of 4 int8 Linear layers [16384 -> 16384], weights
-~ N(0, 0.01) quantized per output channel and column-sharded over the N ranks
-(Shard(1) of the reference's [in, out] weight), activations fp32
-[8192, 16384] ~ N(0, 1) row-sharded over the ranks and quantized per tensor.
-One step = one forward of the stack over the 8192-token batch: each rank
-quantizes its input rows (global absmax by an NCCL MAX all-reduce), the int8
-codes are all-gathered in row chunks while the first layer's GEMM consumes the
-chunks already present, and between layers the GEMM epilogues' absmax is
-all-reduced, each rank quantizes its output columns and the codes are
-all-gathered (again chunk by chunk, overlapped with the next GEMM).  Total
-work is fixed as N grows ("strong" scaling); N = 1 runs the same stack on one
-GPU with no collective.  Inputs are larger than L2 (weights 1 GiB of int8
-codes, input 512 MiB fp32).
+~ N(0, 0.01) quantized per output channel and column-sharded (Shard(1) of the
+reference's [in, out] weight) within groups of tp ranks (tp = N up to 4
+GPUs, 4 at 8: two row groups), activations fp32 [8192, 16384] ~ N(0, 1)
+row-sharded and quantized per tensor with the absmax all-reduced over every
+rank.  One step = one forward of the stack over the 8192-token batch: each
+rank quantizes its input rows, the int8 codes reach the other ranks of its
+group in row chunks (copy-engine pulls from IPC-shared buffers by default,
+or NCCL all-gathers) while each layer's GEMM consumes the chunks already
+present, and between layers the GEMM epilogues' absmax is all-reduced and
+each rank quantizes its output columns for the next exchange.  Total work is
+fixed as N grows ("strong" scaling); N = 1 runs the same stack on one GPU
+with no exchange.  Inputs are larger than L2 (weights 1 GiB of int8 codes,
+input 512 MiB fp32).
 
 At N = 1 the line also carries, under "kernels", config 2 (one per-channel
 Linear [4096 -> 4096] over 2048 tokens: activation quantize + int8 GEMM) and
