@@ -969,8 +969,9 @@ def run_stack(args, rank, world, local_rank, dev):
         "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": STACK_WORKLOAD, "global_batch": M, "seq_len": None,
-                   "parallelism": (f"dp{stack.dp} x tp{stack.tp} (weights column-sharded within groups of "
-                                   f"{stack.tp}, activations row-sharded across them)"),
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"dp{stack.dp} x tp{stack.tp} (weights column-sharded within groups of "
+                                   f"{stack.tp}, activations row-sharded within and across them)"),
                    "exchange": stack.exchange, "row_chunks": C, "launch": graph_note,
                    "l2": "inputs larger than L2 (weights 1 GiB int8 codes in total, input 512 MiB fp32)"},
         "tops": ops / (ms_per_step / 1e3) / 1e12,
