@@ -387,10 +387,15 @@ def _time_graph(g, reps_per_graph, steps, warmup, local_rank, dev):
     return start.elapsed_time(end) / (n * reps_per_graph), n * reps_per_graph, clk.summary()
 
 
-def _kernel_us(fn, dev, reps=16, replays=8):
+KERNEL_CLOCKS = []  # (kernel entry, NVML clock summary) of each _kernel_us timing
+
+
+def _kernel_us(fn, dev, reps=16, replays=8, name=None):
     """Average device time (us) of one call of fn: a CUDA graph of `reps`
     calls replayed `replays` times back to back, CUDA events around the
-    replays only."""
+    replays only.  The replays repeat until they span at least 20 ms so the
+    NVML sampler sees the clock under this kernel's load; its summary is
+    kept in KERNEL_CLOCKS under `name`."""
     import torch
     g = _graph_of(fn, reps, dev)
     for _ in range(2):
@@ -399,11 +404,20 @@ def _kernel_us(fn, dev, reps=16, replays=8):
     a, b = _events(dev)
     stream = torch.cuda.current_stream(dev)
     a.record(stream)
-    for _ in range(replays):
-        g.replay()
+    g.replay()
     b.record(stream)
     torch.cuda.synchronize()
+    per_replay = max(a.elapsed_time(b), 1e-3)
+    replays = max(replays, min(int(20.0 / per_replay) + 1, 4000))
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        a.record(stream)
+        for _ in range(replays):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
     del g
+    if name:
+        KERNEL_CLOCKS.append((name, clk.summary()))
     return a.elapsed_time(b) / (reps * replays) * 1e3
 
 
@@ -665,7 +679,7 @@ def measure_kernels(args, rank, world, local_rank, dev):
         a, b, rs_, cs_, y = sets[nxt(2)]
         _ok(lib.kz_gemm_i8(a.data_ptr(), b.data_ptr(), n, n, n, n, rs_.data_ptr(), 1, cs_.data_ptr(), 1, None, 0,
                            y.data_ptr(), None, n, None, _sh(dev)))
-    us = _kernel_us(gemm8k, dev, reps=4, replays=6)
+    us = _kernel_us(gemm8k, dev, reps=4, replays=6, name="gemm_8192_cubed")
     tops = 2.0 * n ** 3 / (us / 1e6) / 1e12
     out["gemm_8192_cubed"] = {"kernel": "gemm_i8_kernel", "bound": "tensor", "avg_us": us, "achieved": tops,
                               "peak": int8_peak, "unit": "TOP/s", "frac": tops / int8_peak,
@@ -680,7 +694,7 @@ def measure_kernels(args, rank, world, local_rank, dev):
     def w8a32():
         _ok(lib.kz_qlinear_w8a32_f32(xw[nxt(2)].data_ptr(), M_TOK, K_IN, qw.data_ptr(), 0.02 / 127, None, N_OUT, 0,
                                      yw.data_ptr(), _sh(dev)))
-    us = _kernel_us(w8a32, dev, reps=2, replays=3)
+    us = _kernel_us(w8a32, dev, reps=2, replays=3, name="w8a32_qlinear_config2")
     flops = 2.0 * M_TOK * N_OUT * K_IN
     props = torch.cuda.get_device_properties(dev)
     fp32_peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12
@@ -701,7 +715,7 @@ def measure_kernels(args, rank, world, local_rank, dev):
     def deq():
         j = nxt(NSETS)
         _ok(lib.kz_dequantize_i8_f32(qs[j].data_ptr(), nd, 0.01, ds[j].data_ptr(), _sh(dev)))
-    out["dequantize"] = _hbm_entry("dequantize_kernel", _kernel_us(deq, dev), 5.0 * nd, hbm_gbs,
+    out["dequantize"] = _hbm_entry("dequantize_kernel", _kernel_us(deq, dev, name="dequantize"), 5.0 * nd, hbm_gbs,
                                    "5 B/element (1 B code in, 4 B fp32 out)", dram_bytes=5.0 * nd)
     del qs, ds
     # per-channel weight quantize, config 2's 4096 x 4096 weight (absmax_cols4 + quantize_cols4)
@@ -715,7 +729,7 @@ def measure_kernels(args, rank, world, local_rank, dev):
         _ok(lib.kz_quantize_cols_f32(ws[nxt(NSETS)].data_ptr(), K_IN, N_OUT, qT.data_ptr(), s64.data_ptr(),
                                      s32.data_ptr(), wsb.data_ptr(), wsb.numel(), _sh(dev)))
     ne = K_IN * N_OUT
-    out["quantize_cols"] = _hbm_entry("absmax_cols4_kernel + quantize_cols4_kernel", _kernel_us(qcols, dev),
+    out["quantize_cols"] = _hbm_entry("absmax_cols4_kernel + quantize_cols4_kernel", _kernel_us(qcols, dev, name="quantize_cols"),
                                       9.0 * ne, hbm_gbs,
                                       "9 B/element for the pair (absmax 4, quantize 4 + 1); the quantize pass "
                                       "may re-read the 67 MB weight from L2", dram_bytes=5.0 * ne)
@@ -731,10 +745,13 @@ def measure_kernels(args, rank, world, local_rank, dev):
         j = nxt(16)
         _ok(lib.kz_layernorm_partials_f32(lx[j].data_ptr(), Ml, Dl, gm.data_ptr(), bt.data_ptr(), 1e-5,
                                           ly[j].data_ptr(), lp.data_ptr(), _sh(dev)))
-    out["layernorm"] = _hbm_entry("layernorm_partials_kernel", _kernel_us(lnorm, dev), 8.0 * Ml * Dl, hbm_gbs,
+    out["layernorm"] = _hbm_entry("layernorm_partials_kernel", _kernel_us(lnorm, dev, name="layernorm"), 8.0 * Ml * Dl, hbm_gbs,
                                   "8 B/element (4 in, 4 out); 16 rotating 8 MB sets (128 MB, about L2)")
     del lx, ly
     torch.cuda.empty_cache()
+    for name, clk in KERNEL_CLOCKS:  # the SM clock each kernel's replays ran at
+        if name in out:
+            out[name]["clocks"] = clk
     return out
 
 
@@ -902,7 +919,7 @@ def run_stack(args, rank, world, local_rank, dev):
         _ok(lib.kz_gemm_i8(a_chunk.data_ptr(), qt.kmajor().data_ptr(), mc, n_loc, STACK_D, STACK_D, a_s.data_ptr(),
                            0, qt.scale_f32.data_ptr(), 1, None, 0, ys[j[0] % 2].data_ptr(), None, n_loc, None,
                            _sh(dev)))
-    gemm_us = _kernel_us(gemm_launch, dev, reps=4 * C, replays=4)
+    gemm_us = _kernel_us(gemm_launch, dev, reps=4 * C, replays=4, name="stack_gemm")
     del a_chunk, ys, qt0
     hbm_gbs, bf16, bf16_sus, peak_src = peaks()
     int8_peak = 2.0 * bf16
@@ -983,8 +1000,9 @@ def run_stack(args, rank, world, local_rank, dev):
                      "shape": f"M={mc} N={n_loc} K={STACK_D} (one row chunk of one layer on one rank)",
                      "algorithmic": f"2*M*N*K = {gemm_ops:.3e} op per launch",
                      "peak_source": f"2 x bf16_tflops ({bf16:.1f}, {peak_src}) -- int8 dense = 2x bf16 dense on B200",
-                     "timing": f"CUDA events around 4 replays of a graph of the step's {4 * C} GEMM launches "
-                               "(same shapes and weights) alone, right after the timed region",
+                     "timing": f"CUDA events around replays (at least 20 ms) of a graph of the step's {4 * C} "
+                               "GEMM launches (same shapes and weights) alone, right after the timed region",
+                     "clocks": dict(KERNEL_CLOCKS).get("stack_gemm"),
                      "in_step": in_step},
         "phases_ms": phases,
         "output_checksum": checksum,
