@@ -645,6 +645,74 @@ def _e2e_loop(forward, x_host, y_host, x_dev, steps, world, dev):
     return ms
 
 
+def _copies_only_ms(x_host, y_host, x_dev, y_dev, steps, world, dev):
+    """The e2e loop's host copies alone (the same pinned buffers, streams and
+    sizes, no forward): device ms for `steps` steps, max over ranks.  When it
+    is close to the e2e time, the host links, not the GPU, bound the e2e."""
+    import torch
+    import torch.distributed as dist
+    NB = len(x_host)
+    stream = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = _events(dev)
+    e0.record(stream)
+    s_in.wait_stream(stream)
+    s_out.wait_stream(stream)
+    for i in range(steps):
+        b = i % NB
+        with torch.cuda.stream(s_in):
+            x_dev[b].copy_(x_host[b], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            y_host[b].copy_(y_dev, non_blocking=True)
+    stream.wait_stream(s_in)
+    stream.wait_stream(s_out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+class _GpuLocalCpus:
+    """Binds the calling thread to the CPUs NVML reports as local to the GPU
+    (nvmlDeviceGetCpuAffinity, read-only) for the duration of the block, so
+    pinned host buffers allocated inside it land on the GPU's NUMA node and
+    the launching thread runs there; restores the previous affinity after."""
+
+    def __init__(self, local_rank):
+        self.local_rank, self.prev, self.cpus, self.note = local_rank, None, None, "not bound"
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.local_rank)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+            cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+            self.prev = os.sched_getaffinity(0)
+            cpus &= self.prev
+            if cpus:
+                os.sched_setaffinity(0, cpus)
+                self.cpus = sorted(cpus)
+                self.note = f"{len(cpus)} GPU-local CPUs ({self.cpus[0]}..{self.cpus[-1]})"
+        except Exception as e:  # no NVML, or no affinity information: leave the thread as it is
+            self.note = f"not bound ({type(e).__name__})"
+        return self
+
+    def __exit__(self, *a):
+        if self.prev is not None:
+            try:
+                os.sched_setaffinity(0, self.prev)
+            except OSError:
+                pass
+
+
 # ----------------------------------------------- per-kernel HBM rooflines
 
 def measure_kernels(args, rank, world, local_rank, dev):
@@ -943,10 +1011,6 @@ def run_stack(args, rank, world, local_rank, dev):
     rows = stack.input_rows(M) if pipelined else [(0, M)]
     m_loc = sum(b - a for a, b in rows)
     rs = np.random.RandomState(2000 + rank)
-    x_host = [torch.from_numpy(rs.standard_normal((m_loc, STACK_D)).astype(np.float32)).pin_memory()
-              for _ in range(NB)]
-    y_host = [torch.empty((M // stack.dp, n_loc), dtype=torch.float32).pin_memory() for _ in range(NB)]
-    x_dev = [torch.empty((m_loc, STACK_D), dtype=torch.float32, device=dev) for _ in range(NB)]
     del x_local
     torch.cuda.empty_cache()
 
@@ -954,12 +1018,27 @@ def run_stack(args, rank, world, local_rank, dev):
         return (stack.forward_local(xd, M) if pipelined else stack(xd)).data
 
     _stage("stack: e2e")
-    e2e_ms = _e2e_loop(forward_host_rows, x_host, y_host, x_dev, args.e2e_steps, world, dev)
+    with _GpuLocalCpus(local_rank) as numa:
+        x_host = [torch.from_numpy(rs.standard_normal((m_loc, STACK_D)).astype(np.float32)).pin_memory()
+                  for _ in range(NB)]
+        y_host = [torch.empty((M // stack.dp, n_loc), dtype=torch.float32).pin_memory() for _ in range(NB)]
+        x_dev = [torch.empty((m_loc, STACK_D), dtype=torch.float32, device=dev) for _ in range(NB)]
+        e2e_ms = _e2e_loop(forward_host_rows, x_host, y_host, x_dev, args.e2e_steps, world, dev)
+        y_dev = torch.empty(y_host[0].shape, dtype=torch.float32, device=dev)
+        copy_ms = _copies_only_ms(x_host, y_host, x_dev, y_dev, args.e2e_steps, world, dev)
+    in_b, out_b = m_loc * STACK_D * 4, (M // stack.dp) * n_loc * 4
     e2e = {"value": M / (e2e_ms / args.e2e_steps / 1e3), "unit": "tokens/s",
-           "h2d_bytes_per_step": m_loc * STACK_D * 4 * world,
-           "d2h_bytes_per_step": (M // stack.dp) * n_loc * 4 * world,
-           "note": "bytes summed over ranks: each rank uploads its input rows and downloads its output columns"}
-    del x_host, y_host, x_dev
+           "h2d_bytes_per_step": in_b * world, "d2h_bytes_per_step": out_b * world,
+           "ms_per_step": e2e_ms / args.e2e_steps,
+           "note": "bytes summed over ranks: each rank uploads its input rows and downloads its output columns",
+           "host_copies_only": {
+               "ms_per_step": copy_ms / args.e2e_steps,
+               "h2d_gbs_per_rank": in_b / (copy_ms / args.e2e_steps / 1e3) / 1e9,
+               "d2h_gbs_per_rank": out_b / (copy_ms / args.e2e_steps / 1e3) / 1e9,
+               "note": "the same pinned copies, streams and sizes with no forward, all ranks at once (max over "
+                       "ranks): the floor the host links put under the e2e step"},
+           "host_threads": numa.note}
+    del x_host, y_host, x_dev, y_dev
     torch.cuda.empty_cache()
 
     kernels = None
