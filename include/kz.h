@@ -135,6 +135,35 @@ int kz_add_layernorm_partials_f32(const float* x, const float* res, int64_t M, i
                                   const float* beta, float eps, float* sum_out, float* y, uint32_t* partials,
                                   kz_stream_t stream);
 
+/* Scaled dot-product attention, fp32, in the reference's operation order
+ * (replaces the Tensor-op composition of MultiHeadAttention.forward,
+ * python/kansai/nn.py:410-427, between the projections):
+ *   s[i][j] = (sum_t q[i][t] * k[j][t]) * scale     t ascending, no FMA
+ *   s[i][j] = s[i][j] + mask[i][j]                   (mask may be NULL)
+ *   e = exp(s - max_j s);  w = e * (1 / sum_j e)     j ascending
+ *   out[i][t] = sum_j w[i][j] * v[j][t]              j ascending, no FMA
+ * every operation an fp32 round-to-nearest step; exp is the correctly rounded
+ * fp32 exponential (the host libm's expf, which the reference calls, agrees
+ * with it except on rare near-halfway inputs).
+ * Layouts (floats): q(b, h, i, t) = q[(b * seq_q + i) * q_row_stride + h * d_k + t],
+ * k and v the same with seq_k; out(b, i, h * d_k + t) =
+ * out[(b * seq_q + i) * out_row_stride + h * d_k + t] (heads merged);
+ * mask(b, h, i, j) = mask[b * mask_batch_stride + h * mask_head_stride +
+ * i * mask_row_stride + j] (0 strides broadcast).  causal != 0 (needs
+ * seq_q == seq_k) gives keys j > i weight 0 -- causal_mask()'s -1e9 entries --
+ * and ignores mask.  d_k in {32, 64, 128}; q, k, v, out 16-byte aligned, row
+ * strides multiples of 4; seq_k limited by the on-chip score rows
+ * (kz_attention_smem_bytes returns 0 past it).  absmax_partials (may be NULL):
+ * partial maxima of |out| in the KZ_PARTIALS_WORDS format. */
+int kz_attention_f32(const float* q, const float* k, const float* v, int64_t batch, int64_t heads, int64_t seq_q,
+                     int64_t seq_k, int64_t d_k, int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                     const float* mask, int64_t mask_batch_stride, int64_t mask_head_stride, int64_t mask_row_stride,
+                     int causal, float scale, float* out, int64_t out_row_stride, uint32_t* absmax_partials,
+                     kz_stream_t stream);
+/* Dynamic shared memory kz_attention_f32 needs for seq_k keys of d_k, or 0
+ * when that exceeds what one CTA can hold. */
+int kz_attention_smem_bytes(int64_t seq_k, int64_t d_k);
+
 /* Per-output-channel quantize of a reference-layout weight w[K, N] (row-major,
  * nn.py:74-81: [in_features, out_features]); channel n is column n.  Writes
  * K-major codes qT[N, K], scales[N] (double) and scales_f32[N].  Each column

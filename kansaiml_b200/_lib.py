@@ -39,6 +39,9 @@ SIGNATURES = {
     "kz_quantize_tensor_f32": (_I, [_P, _I64, _P, _P, _P, _P, _P]),
     "kz_layernorm_partials_f32": (_I, [_P, _I64, _I64, _P, _P, _F, _P, _P, _P]),
     "kz_add_layernorm_partials_f32": (_I, [_P, _P, _I64, _I64, _P, _P, _F, _P, _P, _P, _P]),
+    "kz_attention_f32": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64,
+                              _I, _F, _P, _I64, _P, _P]),
+    "kz_attention_smem_bytes": (_I, [_I64, _I64]),
     "kz_quantize_cols_workspace_bytes": (_SZ, [_I64, _I64]),
     "kz_quantize_cols_f32": (_I, [_P, _I64, _I64, _P, _P, _P, _P, _SZ, _P]),
     "kz_quantize_cols_f32_noalloc": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),

@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from .quantize import QActivation, QLinear, layernorm_partials_device, partials_buffer
+from .quantize import QActivation, QLinear, attention_device, layernorm_partials_device, partials_buffer
 from .tensor import Tensor, as_tensor, from_flat, ones, randn, zeros
 
 
@@ -133,7 +133,10 @@ class MultiHeadAttention(Module):
     per-channel weight, self-attention (query, key and value the same input)
     runs the three input projections as ONE int8 GEMM over the concatenated
     [d, 3d] weight: per-channel codes and scales are per column, so each
-    column is the same as its separate projection's, bit for bit."""
+    column is the same as its separate projection's, bit for bit.  The
+    attention between the projections is one kz_attention_f32 kernel that
+    takes the reference's own operation order (scores, scale, mask, max, exp,
+    ordered sum, reciprocal, ordered weighted sum of v, nn.py:410-423)."""
 
     def __init__(self, d_model, num_heads, seed=0, device=None):
         if d_model % num_heads:
@@ -169,38 +172,40 @@ class MultiHeadAttention(Module):
         if isinstance(query, QActivation):
             raise ValueError("a pre-quantized input needs the fused self-attention path")
         q_in, k_in, v_in = as_tensor(query), as_tensor(key), as_tensor(value)
-        b, sq, _ = q_in.shape
-        _, sk, _ = k_in.shape
-        h, dk = self.num_heads, self.d_k
-        q = self._proj(q_in, 0, self.w_q).data.reshape(b, sq, h, dk).transpose(1, 2)
-        k = self._proj(k_in, 1, self.w_k).data.reshape(b, sk, h, dk).transpose(1, 2)
-        v = self._proj(v_in, 2, self.w_v).data.reshape(b, sk, h, dk).transpose(1, 2)
-        scores = torch.matmul(q, k.transpose(2, 3)) * (1.0 / math.sqrt(dk))
-        if mask is not None:
-            scores = scores + as_tensor(mask).data
-        att = torch.matmul(torch.softmax(scores, 3), v)
-        merged = Tensor(att.transpose(1, 2).reshape(b, sq, self.d_model).contiguous())
-        return self._proj(merged, 3, self.w_o)
+        q = self._proj(q_in, 0, self.w_q).data
+        k = self._proj(k_in, 1, self.w_k).data
+        v = self._proj(v_in, 2, self.w_v).data
+        causal = self._causal(mask, q.shape[1], k.shape[1])
+        m = as_tensor(mask).data if mask is not None and not causal else None
+        att, _ = attention_device(q, k, v, self.num_heads, mask=m, causal=causal)
+        return self._proj(Tensor(att), 3, self.w_o)
+
+    @staticmethod
+    def _causal(mask, sq, sk):
+        """A causal_mask() of exactly this (query, key) length goes to the
+        kernel as the causal flag; any other mask is added to the scores as
+        given, so a wrong-sized one fails to broadcast, as the reference's
+        scores.add(mask) does."""
+        return (getattr(mask, "causal", False) and sq == sk
+                and tuple(as_tensor(mask).shape[-2:]) == (sq, sk))
 
 
     def _self_attention(self, x, mask):
-        """One int8 GEMM for q, k and v, fp32 scaled dot-product attention
-        (softmax(q k^T / sqrt(d_k) + mask) v in one kernel), int8 output
-        projection.  A causal_mask() is passed as is_causal: keys past each
-        query get weight 0, exactly what its -1e9 entries give (every row keeps
-        its own position, so their exponentials underflow to 0), without
-        reading the mask or the key tiles past the diagonal."""
+        """One int8 GEMM for q, k and v; the fp32 attention kernel reads q, k
+        and v straight out of its [b, s, 3d] output and writes the heads-merged
+        result with its absmax partials, so the int8 output projection's
+        quantize is a single pass.  A causal_mask() goes to the kernel as the
+        causal flag: keys past each query get weight 0, exactly what its -1e9
+        entries give (their exponentials are 0), without reading the mask or
+        the key tiles past the diagonal."""
         b, s, _ = x.shape
-        h, dk = self.num_heads, self.d_k
-        qkv = self.qkv(x).data.reshape(b, s, 3, h, dk).permute(2, 0, 3, 1, 4)
-        # is_causal only for a causal mask of exactly this sequence length;
-        # any other mask is added to the scores as given, so a wrong-sized one
-        # fails to broadcast, as the reference's scores.add(mask) does
-        causal = getattr(mask, "causal", False) and tuple(as_tensor(mask).shape[-2:]) == (s, s)
+        d = self.d_model
+        qkv = self.qkv(x).data.reshape(b, s, 3 * d)
+        causal = self._causal(mask, s, s)
         m = as_tensor(mask).data if mask is not None and not causal else None
-        att = torch.nn.functional.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=m, is_causal=causal)
-        merged = Tensor(att.transpose(1, 2).reshape(b, s, self.d_model))
-        return self.q_proj[3](merged)
+        att, partials = attention_device(qkv[:, :, :d], qkv[:, :, d:2 * d], qkv[:, :, 2 * d:], self.num_heads,
+                                         mask=m, causal=causal)
+        return self.q_proj[3](QActivation.from_partials(att, partials))
 
 
 class TransformerBlock(Module):
@@ -260,8 +265,8 @@ class TransformerBlock(Module):
 
 class CausalMask(Tensor):
     """A mask tensor known to be causal_mask()'s (or a leading square slice of
-    one): the fused self-attention passes it on as is_causal instead of reading
-    it."""
+    one): attention passes it on as the kernel's causal flag instead of
+    reading it."""
     __slots__ = ()
     causal = True
 

@@ -26,6 +26,7 @@ to new granularities, quantize.py:35-44 lists them as future work):
   fused into its epilogue.  ``QLinear(linear, per_channel=True)`` uses it.
 """
 import ctypes
+import math
 
 import numpy as np
 import torch
@@ -121,6 +122,59 @@ def layernorm_partials_device(x, weight=None, bias=None, eps=1e-5, partials=None
     _lib.call("kz_add_layernorm_partials_f32", ptr(x), ptr(residual), M, D, ptr(w), ptr(b), float(eps), ptr(total),
               ptr(y), ptr(partials), stream_handle(dev))
     return y, partials, total
+
+
+def _rows_view(t, what):
+    """(batch, seq, features) CUDA fp32 view whose rows are evenly strided and
+    whose features are contiguous: returns its row stride in floats."""
+    if t.dtype != torch.float32 or not t.is_cuda or t.dim() != 3:
+        raise ValueError(f"attention: {what} must be a 3-d fp32 CUDA tensor")
+    if t.shape[2] > 1 and t.stride(2) != 1:
+        raise ValueError(f"attention: {what} needs contiguous features")
+    if t.shape[1] > 1:
+        rs = t.stride(1)
+    else:   # one row per batch: the batch stride is the row stride
+        rs = t.stride(0) if t.shape[0] > 1 else t.shape[2]
+    if t.shape[0] > 1 and t.stride(0) != t.shape[1] * rs:
+        raise ValueError(f"attention: {what}'s batches must follow each other row by row")
+    return rs
+
+
+def attention_device(q, k, v, heads, mask=None, causal=False, partials=None):
+    """softmax(q k^T / sqrt(d_k) + mask) v per head, fp32, in the reference's
+    operation order (kz_attention_f32; MultiHeadAttention.forward,
+    nn.py:410-427).  q [B, Sq, H*d_k], k and v [B, Sk, H*d_k] (views with
+    strided rows allowed, e.g. slices of one fused q|k|v projection); mask
+    additive, broadcastable to [B, H, Sq, Sk]; causal: keys after each query
+    masked, as causal_mask() does (mask then unused).  Returns the
+    heads-merged [B, Sq, H*d_k] output and the absmax partials of it."""
+    dev = q.device
+    B, Sq, D = q.shape
+    Sk = k.shape[1]
+    if D % heads:
+        raise ValueError(f"attention: {D} features do not split into {heads} heads")
+    if tuple(k.shape) != (B, Sk, D) or tuple(v.shape) != (B, Sk, D):
+        raise ValueError(f"attention: q {list(q.shape)}, k {list(k.shape)}, v {list(v.shape)} do not match")
+    dk = D // heads
+    qrs, krs, vrs = _rows_view(q, "q"), _rows_view(k, "k"), _rows_view(v, "v")
+    if partials is None:
+        partials = partials_buffer(dev)
+    out = torch.empty((B, Sq, D), dtype=torch.float32, device=dev)
+    m, ms = None, (0, 0, 0)
+    if mask is not None and not causal:
+        m = mask.to(device=dev, dtype=torch.float32)
+        try:
+            m = m.expand(B, heads, Sq, Sk)
+        except RuntimeError as e:
+            raise ValueError(f"attention: mask {list(mask.shape)} does not broadcast to "
+                             f"{[B, heads, Sq, Sk]}") from e
+        if Sk > 1 and m.stride(3) != 1:
+            m = m.contiguous()
+        ms = (m.stride(0), m.stride(1), m.stride(2))
+    scale = float(np.float32(1.0 / math.sqrt(dk)))   # nn.py:414: from_flat([1 / sqrt(d_k)])
+    _lib.call("kz_attention_f32", ptr(q), ptr(k), ptr(v), B, heads, Sq, Sk, dk, qrs, krs, vrs, ptr(m), *ms,
+              int(bool(causal)), scale, ptr(out), D, ptr(partials), stream_handle(dev))
+    return out, partials
 
 
 def absmax_partials_device(x, partials=None):

@@ -4,6 +4,7 @@ Every function here is a checker for the CUDA library; see kz_oracle.c for the
 reference file:line each one restates.  Arrays are numpy, C-contiguous.
 """
 import ctypes
+import math
 import os
 import subprocess
 
@@ -41,6 +42,9 @@ def lib():
         L.kzo_gemm_i8_i32.argtypes = [P, P, P, I64, I64, I64, I]
         L.kzo_epilogue_f32.argtypes = [P, I64, I64, P, I64, P, I64, P, I, P]
         L.kzo_layernorm_f32.argtypes = [P, P, I64, I64, P, P, ctypes.c_float, P, P]
+        L.kzo_expf_f32.argtypes = [P, I64, P]
+        L.kzo_attention_f32.argtypes = [P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, P, I64, I64, I64, I,
+                                        ctypes.c_float, P, I64, I]
         _lib = L
     return _lib
 
@@ -199,3 +203,34 @@ def layernorm(x, gamma=None, beta=None, eps=1e-5, residual=None):
     total = np.empty(x.shape, np.float32) if r is not None else None
     lib().kzo_layernorm_f32(_p(x), _p(r), M, D, _p(g), _p(b), float(np.float32(eps)), _p(total), _p(y))
     return y if r is None else (y, total)
+
+
+def attention(q, k, v, heads, mask=None, causal=False, exp="rn"):
+    """The reference's scaled dot-product attention core (nn.py:410-423 composed
+    from Tensor ops, kz_oracle.c): q [B, Sq, H*dk], k and v [B, Sk, H*dk],
+    heads split along the last axis; returns the heads-merged [B, Sq, H*dk].
+    mask: additive, broadcastable to [B, H, Sq, Sk]; causal: keys j > i masked
+    (-1e9).  exp: "rn" the correctly rounded fp32 exp (the CUDA kernel's),
+    "libm" the host's expf (the reference's std::exp)."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    B, Sq, D = q.shape
+    Sk = k.shape[1]
+    dk = D // heads
+    out = np.empty((B, Sq, D), np.float32)
+    m = None
+    strides = (0, 0, 0)
+    if mask is not None and not causal:
+        m = np.ascontiguousarray(np.broadcast_to(_f32(mask), (B, heads, Sq, Sk)))
+        strides = (heads * Sq * Sk, Sq * Sk, Sk)
+    scale = float(np.float32(1.0 / math.sqrt(dk)))      # nn.py:414, from_flat of a Python float
+    lib().kzo_attention_f32(_p(q), _p(k), _p(v), B, heads, Sq, Sk, dk, D, D, D, _p(m), *strides, int(causal),
+                            scale, _p(out), D, 1 if exp == "libm" else 0)
+    return out
+
+
+def expf_host(x):
+    """The host libm's expf of every element (the reference's exp_fwd)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().kzo_expf_f32(_p(x), x.size, _p(out))
+    return out

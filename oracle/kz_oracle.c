@@ -302,3 +302,72 @@ void kzo_layernorm_f32(const float* x, const float* res, int64_t M, int64_t D, c
     free(row);
     free(cen);
 }
+
+/* Scaled dot-product attention as the reference composes it in
+ * MultiHeadAttention.forward (python/kansai/nn.py:410-427) from its Tensor
+ * ops, one (batch, head) at a time:
+ *   scores = q.matmul(k^T)      Ops.cpp:328-337: +0.0f, then += q*k, t ascending
+ *   .mul(scale)                 fp32 multiply
+ *   .add(mask)                  optional, broadcast by the strides
+ *   .softmax(3)                 Tensor.cpp:906-913: max over the row (Ops.cpp:
+ *                               275-292), sub, exp, sum (reduce_to_shape,
+ *                               Ops.cpp:177-190: +0.0f, += e, j ascending),
+ *                               div = mul by 1.0f/sum (Tensor.cpp:677-679)
+ *   weights.matmul(v)           +0.0f, += w*v, j ascending
+ * exp_mode 0: the correctly rounded fp32 exp (exp in double, narrowed), the
+ * one the CUDA kernel computes; 1: the host libm's expf, the one the reference
+ * calls (std::exp on a float).  causal: keys j > i masked, as causal_mask()'s
+ * -1e9 entries do (given here as the flag; the reference adds the mask, and
+ * every such key's exp is exactly 0).  Layouts as kz_attention_f32's. */
+void kzo_attention_f32(const float* q, const float* k, const float* v, int64_t B, int64_t H, int64_t Sq,
+                       int64_t Sk, int64_t dk, int64_t q_rs, int64_t k_rs, int64_t v_rs, const float* mask,
+                       int64_t m_bs, int64_t m_hs, int64_t m_rs, int causal, float scale, float* out,
+                       int64_t o_rs, int exp_mode) {
+    float* s = (float*)malloc((size_t)(Sk > 0 ? Sk : 1) * sizeof(float));
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t i = 0; i < Sq; ++i) {
+                const float* qi = q + (b * Sq + i) * q_rs + h * dk;
+                for (int64_t j = 0; j < Sk; ++j) {
+                    const float* kj = k + (b * Sk + j) * k_rs + h * dk;
+                    float acc = 0.0f;
+                    for (int64_t t = 0; t < dk; ++t) {
+                        const float p = qi[t] * kj[t];
+                        acc = acc + p;
+                    }
+                    float sc = acc * scale;
+                    if (causal)
+                        sc = sc + (j > i ? -1e9f : 0.0f);
+                    else if (mask)
+                        sc = sc + mask[b * m_bs + h * m_hs + i * m_rs + j];
+                    s[j] = sc;
+                }
+                float m = s[0];
+                for (int64_t j = 1; j < Sk; ++j)
+                    if (s[j] > m) m = s[j];
+                float den = 0.0f;
+                for (int64_t j = 0; j < Sk; ++j) {
+                    const float x = s[j] - m;
+                    s[j] = exp_mode ? expf(x) : (float)exp((double)x);
+                    den = den + s[j];
+                }
+                const float r = 1.0f / den;
+                for (int64_t j = 0; j < Sk; ++j) s[j] = s[j] * r;
+                float* oi = out + (b * Sq + i) * o_rs + h * dk;
+                for (int64_t t = 0; t < dk; ++t) {
+                    float acc = 0.0f;
+                    for (int64_t j = 0; j < Sk; ++j) {
+                        const float p = s[j] * v[(b * Sk + j) * v_rs + h * dk + t];
+                        acc = acc + p;
+                    }
+                    oi[t] = acc;
+                }
+            }
+    free(s);
+}
+
+/* The host libm's expf, elementwise: what the reference's exp_fwd
+ * (Ops.cpp:221-223, std::exp on a float) computes. */
+void kzo_expf_f32(const float* x, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = expf(x[i]);
+}

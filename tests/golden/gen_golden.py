@@ -29,6 +29,9 @@ Fixtures:
                       parameters, of x and of x.add(residual), and the
                       quantize_symmetric codes of the result (config 3's
                       LayerNorm -> quantize prologue).
+  attention_cases.npz nn.MultiHeadAttention.forward (nn.py:410-427) with
+                      identity projections: the attention core with the causal
+                      mask, a broadcast additive mask, and none.
 """
 import os
 import sys
@@ -193,6 +196,26 @@ def layernorm_cases():
     print("layernorm_cases.npz:", len(inputs.LAYERNORM_SHAPES), "shapes")
 
 
+def attention_cases():
+    """The reference's own MultiHeadAttention.forward (nn.py:410-427) with its
+    four projections set to the identity: q, k, v and the merged output pass
+    through them unchanged (each projection sum has one non-zero term), so the
+    output is the attention core -- scores, scale, mask, softmax, weighted sum
+    -- exactly as the reference composes it."""
+    out = {}
+    for i, (B, Sq, Sk, D, H, kind) in enumerate(inputs.ATTENTION_CASES):
+        q, k, v, mask = inputs.attention_inputs(i)
+        mha = nn.MultiHeadAttention(D, H)
+        eye = from_np(np.eye(D, dtype=np.float32))
+        mha.w_q = mha.w_k = mha.w_v = mha.w_o = eye
+        y = mha.forward(from_np(q), from_np(k), from_np(v), mask=from_np(mask) if mask is not None else None)
+        out[f"c{i}__inputs_sha256"] = np.asarray(sha(q) + sha(k) + sha(v) + (sha(mask) if mask is not None else ""))
+        out[f"c{i}__y"] = to_np(y)
+    out["count"] = np.int64(len(inputs.ATTENTION_CASES))
+    np.savez_compressed(os.path.join(HERE, "attention_cases.npz"), **out)
+    print("attention_cases.npz:", len(inputs.ATTENTION_CASES), "cases")
+
+
 if __name__ == "__main__":
     quantize_cases()
     percol_cases()
@@ -201,3 +224,4 @@ if __name__ == "__main__":
     xor_qlinear()
     chunk_cases()
     layernorm_cases()
+    attention_cases()

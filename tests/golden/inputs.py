@@ -100,3 +100,29 @@ def layernorm_inputs(i):
     gamma = rs.uniform(0.5, 1.5, d).astype(np.float32)
     beta = (rs.standard_normal(d) * 0.1).astype(np.float32)
     return x, res, gamma, beta
+
+
+# (batch, seq_q, seq_k, d_model, heads, mask kind): self-attention with the
+# causal mask across a 64-row tile edge, cross-attention with a broadcast
+# random additive mask, no mask, and head widths 32 / 64 / 128
+ATTENTION_CASES = [(2, 24, 24, 128, 4, "causal"), (2, 67, 67, 128, 2, "causal"), (1, 5, 70, 64, 2, "mask"),
+                   (3, 9, 130, 32, 1, "none"), (1, 80, 80, 128, 1, "mask")]
+
+
+def attention_inputs(i):
+    """(q, k, v, mask or None) for attention case i: q [B, Sq, D], k and v
+    [B, Sk, D]; the causal mask is causal_mask()'s [1, 1, S, S] (-1e9 above the
+    diagonal), the random one [B, 1, Sq, Sk] with about a third of its
+    entries negative."""
+    B, Sq, Sk, D, H, kind = ATTENTION_CASES[i]
+    rs = np.random.RandomState(700 + i)
+    q = (rs.standard_normal((B, Sq, D)) * 2).astype(np.float32)
+    k = (rs.standard_normal((B, Sk, D)) * 2).astype(np.float32)
+    v = rs.standard_normal((B, Sk, D)).astype(np.float32)
+    if kind == "causal":
+        mask = np.triu(np.full((Sq, Sk), -1e9, np.float32), 1)[None, None]
+    elif kind == "mask":
+        mask = (rs.uniform(-3, 0, (B, 1, Sq, Sk)) * (rs.uniform(size=(B, 1, Sq, Sk)) < 0.3)).astype(np.float32)
+    else:
+        mask = None
+    return q, k, v, mask

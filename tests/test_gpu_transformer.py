@@ -15,18 +15,18 @@ and softmax fp32.
    be bit-exact (GELU layers: 1e-5 relative, CUDA erff).  fc2's input codes,
    quantized from the absmax partials of fc1's epilogue, and every
    LayerNorm's input codes must equal the oracle's exactly.
+   The output projection's input codes -- quantized from the absmax partials
+   the attention kernel emits -- must equal the oracle's attention (the
+   reference's operation order, correctly rounded exp) of the fused q|k|v
+   projection the device computed, quantized: bit for bit.
 3. End to end: the logits are compared with a CPU forward that runs every
-   LayerNorm and Linear through the oracle.  Attention is the one fp32 step
-   not restated in the reference's order: torch's scaled-dot-product kernel
-   (scores q k^T scaled, causal, row softmax with a running max, weighted sum
-   of v, all fp32 with its own summation order) against numpy's fp32
-   matmul / max / exp / sum / divide.  Its few-ulp differences can move an
-   activation across a rounding boundary of the next quantize, so the logits
-   must agree to 2e-3 relative (Frobenius) and in at least 99% of the argmax
-   tokens.
+   LayerNorm, Linear and attention through the oracle.  The one step whose
+   last bits differ is GELU's erf (CUDA's erff on the device, the host libm's
+   in the oracle and the reference; neither is correctly rounded); a one-ulp
+   difference can move an fc1 output across a rounding boundary of fc2's
+   quantize, so the logits must agree to 2e-3 relative (Frobenius) and in at
+   least 99% of the argmax tokens.
 """
-import math
-
 import numpy as np
 import pytest
 import torch
@@ -73,6 +73,14 @@ def test_layerwise_bit_exact(model_and_ids, monkeypatch):
             xq, xs = x
             if i > 0 and calls[i - 1][3] == "gelu":   # fc2: codes from fc1's epilogue partials
                 xq_o, xs_o = ocpu.quantize_tensor(calls[i - 1][4].reshape(xq.shape))
+                assert xs == xs_o, f"call {i}"
+                np.testing.assert_array_equal(xq, xq_o, err_msg=f"call {i}")
+            if i < 8 and i % 4 == 1:   # output projection: codes of the attention kernel's output
+                qkv = calls[i - 1][4].reshape(ids.shape[0], ids.shape[1], -1)
+                d = qkv.shape[-1] // 3
+                att = ocpu.attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], model.heads, causal=True,
+                                     exp="rn")
+                xq_o, xs_o = ocpu.quantize_tensor(att.reshape(xq.shape))
                 assert xs == xs_o, f"call {i}"
                 np.testing.assert_array_equal(xq, xq_o, err_msg=f"call {i}")
         else:
@@ -214,20 +222,20 @@ def test_add_layernorm_equals_add_then_layernorm(cuda_device):
 
 
 def test_causal_flag_matches_the_explicit_mask(cuda_device):
-    """causal_mask() reaches attention as is_causal.  Its -1e9 entries give
-    weight exactly 0 (every row keeps its own position, so the shifted
-    exponentials underflow), so the result agrees with the explicit mask's to
-    fp32 rounding."""
+    """causal_mask() reaches the attention kernel as its causal flag.  Its
+    -1e9 entries give exponentials of exactly 0, so the explicit mask -- every
+    key read, masked ones included -- gives the same bits."""
     from kansaiml_b200 import nn as knn
+    from kansaiml_b200 import quantize as kq
     g = torch.Generator(device="cuda")
     g.manual_seed(1)
-    q, k, v = (torch.randn((4, 4, 256, 64), device="cuda", generator=g) for _ in range(3))
+    q, k, v = (torch.randn((4, 256, 256), device="cuda", generator=g) for _ in range(3))
     mask = knn.causal_mask(256, device="cuda")
     assert getattr(mask, "causal", False)
-    sdpa = torch.nn.functional.scaled_dot_product_attention
-    flagged = sdpa(q, k, v, is_causal=True)
-    explicit = sdpa(q, k, v, attn_mask=mask.data)
-    torch.testing.assert_close(flagged, explicit, rtol=1e-5, atol=1e-6)
+    assert knn.MultiHeadAttention._causal(mask, 256, 256) and not knn.MultiHeadAttention._causal(mask, 128, 128)
+    flagged, _ = kq.attention_device(q, k, v, 4, causal=True)
+    explicit, _ = kq.attention_device(q, k, v, 4, mask=mask.data)
+    assert torch.equal(flagged, explicit)
 
 
 def _ln(x, eps=1e-5):
@@ -241,20 +249,10 @@ def _linear(x, w, bias=None, act=0):
     return y.reshape(shape[:-1] + (w.shape[1],))
 
 
-def _attention(h, w, heads, mask):
-    b, s, d = h.shape
-    dk = d // heads
-
-    def split(t):
-        return t.reshape(b, s, heads, dk).transpose(0, 2, 1, 3)
-
-    q, k, v = (split(_linear(h, w[n])) for n in ("w_q", "w_k", "w_v"))
-    scores = np.matmul(q, k.transpose(0, 1, 3, 2)) * np.float32(1.0 / math.sqrt(dk)) + mask
-    scores = scores - scores.max(-1, keepdims=True)
-    p = np.exp(scores)
-    p = p / p.sum(-1, keepdims=True)
-    att = np.matmul(p, v).transpose(0, 2, 1, 3).reshape(b, s, d)
-    return _linear(np.ascontiguousarray(att, dtype=np.float32), w["w_o"])
+def _attention(h, w, heads):
+    q, k, v = (_linear(h, w[n]) for n in ("w_q", "w_k", "w_v"))
+    att = ocpu.attention(q, k, v, heads, causal=True, exp="rn")
+    return _linear(att, w["w_o"])
 
 
 def test_end_to_end_vs_oracle(model_and_ids):
@@ -264,10 +262,9 @@ def test_end_to_end_vs_oracle(model_and_ids):
     idn = ids.cpu().numpy()
     s = idn.shape[1]
     x = (f["tok"][idn] + f["pos"][:s]).astype(np.float32)
-    mask = np.triu(np.full((s, s), -1e9, np.float32), 1)
     for w in f["blocks"]:
         h = _ln(x)
-        x = x + _attention(h, w, model.heads, mask)
+        x = x + _attention(h, w, model.heads)
         h = _ln(x)
         h = _linear(h, w["fc1"], w["fc1_b"], act=2)
         x = x + _linear(h, w["fc2"], w["fc2_b"])

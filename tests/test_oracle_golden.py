@@ -128,6 +128,63 @@ def test_layernorm_bit_exact_vs_reference():
         np.testing.assert_array_equal(q, g[f"c{i}__q"], err_msg=str(i))
 
 
+def _attention_case(i, exp):
+    B, Sq, Sk, D, H, kind = inputs.ATTENTION_CASES[i]
+    q, k, v, mask = inputs.attention_inputs(i)
+    if kind == "causal":
+        return ocpu.attention(q, k, v, H, causal=True, exp=exp)
+    return ocpu.attention(q, k, v, H, mask=mask, exp=exp)
+
+
+def test_attention_bit_exact_vs_reference():
+    """The oracle's attention core with the host's expf (the function the
+    reference's std::exp calls) against the reference's own
+    MultiHeadAttention.forward with identity projections: bit for bit, the
+    causal mask given as the flag included (its keys' exponentials are 0)."""
+    g = golden("attention_cases.npz")
+    for i in range(int(g["count"])):
+        q, k, v, mask = inputs.attention_inputs(i)
+        assert inputs.sha(q) + inputs.sha(k) + inputs.sha(v) + (inputs.sha(mask) if mask is not None else "") == \
+            str(g[f"c{i}__inputs_sha256"])
+        assert _attention_case(i, "libm").tobytes() == g[f"c{i}__y"].tobytes(), i
+        if inputs.ATTENTION_CASES[i][5] == "causal":   # the explicit mask gives the same bits
+            H = inputs.ATTENTION_CASES[i][4]
+            assert ocpu.attention(q, k, v, H, mask=mask, exp="libm").tobytes() == g[f"c{i}__y"].tobytes(), i
+
+
+def test_attention_rounded_exp_vs_reference():
+    """With the correctly rounded exp (the CUDA kernel's), the oracle differs
+    from the reference only where the host's expf is not correctly rounded:
+    a handful of outputs, by a few ulps."""
+    g = golden("attention_cases.npz")
+    diff = total = 0
+    for i in range(int(g["count"])):
+        y, ref = _attention_case(i, "rn"), g[f"c{i}__y"]
+        bad = y.view(np.int32) != ref.view(np.int32)
+        diff += int(bad.sum())
+        total += y.size
+        np.testing.assert_allclose(y, ref, rtol=2e-6, atol=1e-7, err_msg=str(i))
+    assert diff <= total // 1000, (diff, total)
+
+
+def test_attention_exp_modes_agree_where_expf_rounds_correctly():
+    """The two exp modes of the oracle: the host's expf against the double
+    exp narrowed to fp32 over the softmax's input range -- they differ only on
+    inputs whose exponential lies within a hair of a rounding midpoint, a
+    fraction of a percent."""
+    x = -np.random.RandomState(5).uniform(0, 60, 100000).astype(np.float32)
+    libm = ocpu.expf_host(x)
+    rn = np.exp(x.astype(np.float64)).astype(np.float32)
+    bad = libm.view(np.int32) != rn.view(np.int32)
+    assert bad.sum() <= 200, int(bad.sum())
+    assert np.all(np.abs(libm.view(np.int32).astype(np.int64) - rn.view(np.int32)) <= 1)
+    # every disagreement sits next to a midpoint of the two neighbouring floats
+    exact = np.exp(x[bad].astype(np.float64))
+    lo = np.minimum(libm[bad], rn[bad]).astype(np.float64)
+    hi = np.maximum(libm[bad], rn[bad]).astype(np.float64)
+    assert np.all(np.abs((exact - lo) / (hi - lo) - 0.5) < 0.01)
+
+
 def test_int8_gemm_and_epilogue_small():
     rs = np.random.RandomState(1)
     a = rs.randint(-127, 128, (33, 80)).astype(np.int8)
