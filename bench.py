@@ -775,6 +775,28 @@ def measure_kernels(args, rank, world, local_rank, dev):
                        "instructions per multiply-add: half that",
         "algorithmic": f"2*M*N*K = {flops:.3e} flop per call, per-tensor int8 weight, fp32 activations"}
     del xw, qw, yw
+    # config 3's attention core (batch 32, context 256, 4 heads of 64, causal), reference operation order
+    Ba, Sa, Da, Ha = 32, 256, 256, 4
+    qkvs = [torch.randn((Ba, Sa, 3 * Da), device=dev) for _ in range(4)]
+    att_out = torch.empty((Ba, Sa, Da), device=dev)
+    att_parts = torch.zeros(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+
+    def attn():
+        t = qkvs[nxt(4)]
+        _ok(lib.kz_attention_f32(t.data_ptr(), t.data_ptr() + 4 * Da, t.data_ptr() + 8 * Da, Ba, Ha, Sa, Sa, Da // Ha,
+                                 3 * Da, 3 * Da, 3 * Da, None, 0, 0, 0, 1, 0.125, att_out.data_ptr(), Da,
+                                 att_parts.data_ptr(), _sh(dev)))
+    us = _kernel_us(attn, dev, reps=8, replays=4, name="attention_config3")
+    att_ops = Ba * Ha * (Sa * (Sa + 1) // 2) * 4.0 * (Da // Ha)
+    out["attention_config3"] = {
+        "kernel": "attention_ref_kernel<64>", "bound": "fp32 SIMT (ordered, no FMA)", "avg_us": us,
+        "achieved": att_ops / (us / 1e6) / 1e12, "unit": "Top/s", "peak": fp32_peak / 2,
+        "frac": att_ops / (us / 1e6) / 1e12 / (fp32_peak / 2),
+        "peak_source": "fp32 instruction issue: SMs x 128 lanes x 1.965 GHz (each product and each sum its own "
+                       "instruction, as the reference's loops round them)",
+        "algorithmic": f"{att_ops:.3e} op per call: per (batch, head) S(S+1)/2 causal (query, key) pairs x d_k "
+                       "x (mul + add) for q.k^T and again for w.v"}
+    del qkvs, att_out
     # dequantize, 8.4 M codes (config 2's activation size), 4 rotating sets
     nd = M_TOK * K_IN
     qs = [torch.randint(-127, 128, (nd,), dtype=torch.int8, device=dev) for _ in range(NSETS)]

@@ -51,7 +51,9 @@ constexpr int kAttKeys = 64;      // keys per staged K / V tile
 constexpr int kAttThreads = 128;  // 8 x 16 threads
 constexpr int kAttMaxDk = 128;
 constexpr int kAttMaxBlocks = KZ_PARTIALS_WORDS - 3;
-constexpr size_t kAttMaxSmem = 227 * 1024;
+// opt-in dynamic shared memory ceiling: 227 KB per CTA less room for the
+// kernel's static arrays (the two count together against the limit)
+constexpr size_t kAttMaxSmem = 226 * 1024;
 
 struct AttArgs {
     const float* q;

@@ -28,6 +28,9 @@ int set_error(int code, const std::string& msg) {
 }
 
 int cuda_error(cudaError_t e, const char* what) {
+    // consume the runtime's per-thread last error: a failed non-sticky call
+    // (a bad argument) must not surface again at the next launch check
+    (void)cudaGetLastError();
     return set_error(KZ_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + ": " + cudaGetErrorString(e));
 }
 
