@@ -30,9 +30,13 @@
 // 16-byte reads of 8 consecutive lanes fall in distinct bank groups), keeps
 // the block's whole score rows on chip, runs the softmax there and streams
 // 64-key tiles of V for the weighted sum.  Thread tile 8 query rows x 4 keys
-// (rows ty + 8a, keys tx + 16b): per 4 reduction steps 12 shared 16-byte
-// loads feed 256 fp32 operations.  The next tile's global loads are issued
-// into registers before the current tile's arithmetic.  The output is written
+// (row pairs i, i + 8 with i = ty + 16 rp; keys tx + 16 c).  The arithmetic
+// runs on sm_100's packed f32x2 instructions, one instruction per two rows,
+// each half rounded as the scalar instruction would: query rows and score
+// rows are stored pair-interleaved so their 16-byte loads are the packed
+// operands, and per 4 reduction steps 12 shared loads feed 128 packed
+// instructions (256 fp32 operations).  The next tile's global loads are
+// issued into registers before the current tile's arithmetic.  The output is written
 // head-merged ([batch, seq_q, heads * d_k], the layout the output projection
 // reads) with the absmax partials of every value, so the projection's
 // per-tensor quantize needs no extra pass.
@@ -73,7 +77,37 @@ struct AttArgs {
 __device__ __forceinline__ uint32_t abs_bits_f(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
 
 // exp(x) rounded to nearest fp32 from a double-precision exp.
-__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp((double)x)); }
+// Below -104 the exponential is under half the smallest subnormal and rounds
+// to 0 either way; those inputs (masked scores) skip the double exp.
+__device__ __forceinline__ float exp_rn(float x) {
+    return x < -104.0f ? 0.0f : __double2float_rn(exp((double)x));
+}
+
+// Packed fp32 pairs: sm_100's f32x2 arithmetic rounds each half exactly like
+// the scalar instruction (round to nearest, subnormals kept), so a pair of
+// separately rounded products / sums costs one instruction instead of two.
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk(uint64_t r, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+// d = d + a * b per half, the product rounded before the sum (no FMA)
+__device__ __forceinline__ void mul_add2(uint64_t& d, uint64_t a, uint64_t b) {
+    uint64_t p;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(a), "l"(b));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(d), "l"(p));
+}
+
+// Row pairs.  Query rows i and i + 8 (i = ty + 16 rp) are one pair, id
+// pid = ty + 8 rp; the pair's values are interleaved in shared memory
+// (element (i, x) at pair[2 x + (i / 8) % 2]) so one 16-byte load yields the
+// two rows' values at two consecutive x -- ready-made f32x2 operands.
+__device__ __forceinline__ int pair_id(int i) { return (i & 7) + 8 * (i >> 4); }
+__device__ __forceinline__ int pair_slot(int i) { return (i >> 3) & 1; }
+__device__ __forceinline__ int pair_row(int pid, int slot) { return (pid & 7) + 16 * (pid >> 3) + 8 * slot; }
 
 // Loads rows [r0, r0 + 64) x d_k of one head (row stride rs) as float4s into
 // registers: thread t takes float4 index t + 128 u.  Rows >= nrows read as 0.
@@ -93,6 +127,7 @@ struct TileRegs {
                 r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
+    // row-major tile [64][DK + 4] (K and V)
     __device__ __forceinline__ void store(float* tile) const {
 #pragma unroll
         for (int u = 0; u < F4; ++u) {
@@ -101,24 +136,70 @@ struct TileRegs {
             *reinterpret_cast<float4*>(tile + row * (DK + 4) + 4 * c4) = r[u];
         }
     }
+    // row-pair interleaved tile [32][2 DK + 4] (Q)
+    __device__ __forceinline__ void store_pairs(float* tile) const {
+#pragma unroll
+        for (int u = 0; u < F4; ++u) {
+            const int f = threadIdx.x + u * kAttThreads;
+            const int row = f / (DK / 4), c4 = f % (DK / 4);
+            float* d = tile + pair_id(row) * (2 * DK + 4) + 8 * c4 + pair_slot(row);
+            d[0] = r[u].x;
+            d[2] = r[u].y;
+            d[4] = r[u].z;
+            d[6] = r[u].w;
+        }
+    }
 };
+
+// A[rp][c] = {s[i][j], s[i + 8][j]} += q[.][t] * k[j][t] for t ascending
+// (i = ty + 16 rp, j = tx + 16 c of the tile), each product and sum rounded
+// on its own.  DIAG (causal diagonal tile) skips the pairs rp < c, whose rows
+// all precede their keys.
+template <int DK, bool DIAG>
+__device__ __forceinline__ void score_tile(const float* qp, const float* ks, int ty, int tx, uint64_t (&A)[4][4]) {
+    constexpr int P = DK + 4, PQ = 2 * DK + 4;
+#pragma unroll 2
+    for (int t4 = 0; t4 < DK / 4; ++t4) {
+        float4 qa[4], qb[4], kv[4];
+#pragma unroll
+        for (int rp = 0; rp < 4; ++rp) {
+            const float* row = qp + (ty + 8 * rp) * PQ + 8 * t4;
+            qa[rp] = *reinterpret_cast<const float4*>(row);        // t, t + 1
+            qb[rp] = *reinterpret_cast<const float4*>(row + 4);    // t + 2, t + 3
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (tx + 16 * c) * P + 4 * t4);
+#define KZ_QK_STEP(QV, LO, HI, KC)                                                   \
+        _Pragma("unroll") for (int c = 0; c < 4; ++c) {                              \
+            const uint64_t kd = pk(kv[c].KC, kv[c].KC);                              \
+            _Pragma("unroll") for (int rp = 0; rp < 4; ++rp)                         \
+                if (!DIAG || rp >= c) mul_add2(A[rp][c], pk(QV[rp].LO, QV[rp].HI), kd); \
+        }
+        KZ_QK_STEP(qa, x, y, x)
+        KZ_QK_STEP(qa, z, w, y)
+        KZ_QK_STEP(qb, x, y, z)
+        KZ_QK_STEP(qb, z, w, w)
+#undef KZ_QK_STEP
+    }
+}
 
 template <int DK>
 __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a) {
-    constexpr int P = DK + 4;                   // Q / K / V tile pitch
+    constexpr int P = DK + 4;                   // K / V tile pitch
+    constexpr int PQ = 2 * DK + 4;              // Q row-pair pitch
     constexpr int NC = (DK + 63) / 64;          // output column groups per thread
     extern __shared__ __align__(16) float att_smem[];
-    float* qs = att_smem;                       // [64][P]
-    float* ks = qs + kAttRows * P;              // [64][P], K tiles then V tiles
-    float* ss = ks + kAttKeys * P;              // [64][s_pitch] scores -> weights
+    float* qp = att_smem;                       // [32][PQ] query row pairs
+    float* ks = qp + (kAttRows / 2) * PQ;       // [64][P], K tiles then V tiles
+    float* ss = ks + kAttKeys * P;              // [32][s_pitch] score row pairs -> weights
     __shared__ float s_max[kAttRows];
     __shared__ float s_rinv[kAttRows];
     __shared__ uint32_t red[kAttThreads / 32];
     griddep_launch_dependents();
     griddep_wait();
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;     // keys tx + 16b, rows ty + 8a
-    const int sp = a.s_pitch;
+    const int tx = tid & 15, ty = tid >> 4;     // keys tx + 16c, row pairs ty + 8rp
+    const int sp = a.s_pitch;                   // floats per row pair: 2 x keys + 4
     uint32_t amax = 0;
 
     for (int item = blockIdx.x; item < a.items; item += gridDim.x) {
@@ -130,15 +211,18 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
         // keys this block needs: all of them, or (causal) up to its last row
         const int kend = a.causal ? min(a.seq_k, i0 + rows) : a.seq_k;
         const int ntiles = (kend + kAttKeys - 1) / kAttKeys;
+        const int kpad = ntiles * kAttKeys;
         const float* qg = a.q + (int64_t)b * a.seq_q * a.q_rs + (int64_t)h * DK;
         const float* kg = a.k + (int64_t)b * a.seq_k * a.k_rs + (int64_t)h * DK;
         const float* vg = a.v + (int64_t)b * a.seq_k * a.v_rs + (int64_t)h * DK;
         const float* mg = a.mask ? a.mask + (int64_t)b * a.m_bs + (int64_t)h * a.m_hs : nullptr;
+        // keys row i (of this block) attends to: [0, lim)
+        auto row_lim = [&](int i) { return i < rows ? (a.causal ? min(kend, i0 + i + 1) : kend) : 0; };
 
         TileRegs<DK> pre;
         pre.load(qg, a.q_rs, i0, a.seq_q);
         __syncthreads();                        // the previous item is done with every buffer
-        pre.store(qs);
+        pre.store_pairs(qp);
         pre.load(kg, a.k_rs, 0, kend);
 
         // ---- scores: s[i][j] = ((sum_t q[i][t] * k[j][t]) * scale) (+ mask)
@@ -147,39 +231,30 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
             pre.store(ks);
             __syncthreads();
             if (kt + 1 < ntiles) pre.load(kg, a.k_rs, (kt + 1) * kAttKeys, kend);
-            float acc[8][4];
+            uint64_t A[4][4];
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
+            for (int rp = 0; rp < 4; ++rp)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
-#pragma unroll 2
-            for (int t4 = 0; t4 < DK / 4; ++t4) {
-                float4 qv[8], kv[4];
+                for (int c = 0; c < 4; ++c) A[rp][c] = 0ull;    // +0.0f, +0.0f
+            if (a.causal && kt == ntiles - 1)
+                score_tile<DK, true>(qp, ks, ty, tx, A);
+            else
+                score_tile<DK, false>(qp, ks, ty, tx, A);
 #pragma unroll
-                for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float4*>(qs + (ty + 8 * r) * P + 4 * t4);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (tx + 16 * c) * P + 4 * t4);
-#pragma unroll
-                for (int r = 0; r < 8; ++r)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        float s = acc[r][c];
-                        s = __fadd_rn(s, __fmul_rn(qv[r].x, kv[c].x));
-                        s = __fadd_rn(s, __fmul_rn(qv[r].y, kv[c].y));
-                        s = __fadd_rn(s, __fmul_rn(qv[r].z, kv[c].z));
-                        s = __fadd_rn(s, __fmul_rn(qv[r].w, kv[c].w));
-                        acc[r][c] = s;
-                    }
-            }
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int i = ty + 8 * r;
+            for (int rp = 0; rp < 4; ++rp) {
+                const int pid = ty + 8 * rp, il = pair_row(pid, 0), ih = il + 8;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int j = kt * kAttKeys + tx + 16 * c;
-                    float s = __fmul_rn(acc[r][c], a.scale);
-                    if (mg && i < rows && j < kend) s = __fadd_rn(s, __ldg(mg + (int64_t)(i0 + i) * a.m_rs + j));
-                    ss[i * sp + j] = s;
+                    float lo, hi;
+                    upk(A[rp][c], lo, hi);
+                    lo = __fmul_rn(lo, a.scale);
+                    hi = __fmul_rn(hi, a.scale);
+                    if (mg && j < kend) {
+                        if (il < rows) lo = __fadd_rn(lo, __ldg(mg + (int64_t)(i0 + il) * a.m_rs + j));
+                        if (ih < rows) hi = __fadd_rn(hi, __ldg(mg + (int64_t)(i0 + ih) * a.m_rs + j));
+                    }
+                    *reinterpret_cast<float2*>(ss + pid * sp + 2 * j) = make_float2(lo, hi);
                 }
             }
         }
@@ -187,72 +262,79 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
         pre.load(vg, a.v_rs, 0, kend);
         __syncthreads();
 
-        // ---- softmax over each row's keys j < lim(i): max, exp(s - max), ordered sum, * 1/sum
-        const int kpad = ntiles * kAttKeys;
+        // ---- softmax of each row over its keys [0, lim): max, exp(s - max), ordered sum, * 1/sum
         {
-            // row max, two threads per row (order-free)
-            const int i = tid >> 1, half = tid & 1;
-            const int lim = a.causal ? min(kend, i0 + i + 1) : kend;
-            float m = -INFINITY;
-            bool any = false;
-            for (int j = half; j < lim; j += 2) {
-                const float s = ss[i * sp + j];
-                if (!any || s > m) m = s;
-                any = true;
+            // row-pair max, four threads per pair (order-free)
+            const int pid = tid >> 2, part = tid & 3;
+            const int il = pair_row(pid, 0), ih = il + 8;
+            const int ll = row_lim(il), lh = row_lim(ih);
+            float ml = -INFINITY, mh = -INFINITY;
+            for (int j = part; j < max(ll, lh); j += 4) {
+                const float2 v = *reinterpret_cast<const float2*>(ss + pid * sp + 2 * j);
+                if (j < ll) ml = fmaxf(ml, v.x);
+                if (j < lh) mh = fmaxf(mh, v.y);
             }
-            const float other = __shfl_xor_sync(0xffffffffu, m, 1);
-            const int other_any = __shfl_xor_sync(0xffffffffu, (int)any, 1);
-            if (other_any && (!any || other > m)) m = other;
-            if (half == 0) s_max[i] = m;
-        }
-        __syncthreads();
-        for (int e = tid; e < kAttRows * (kpad / 4); e += kAttThreads) {
-            const int i = e / (kpad / 4), j4 = e % (kpad / 4);
-            const int lim = i < rows ? (a.causal ? min(kend, i0 + i + 1) : kend) : 0;
-            float4* p = reinterpret_cast<float4*>(ss + i * sp + 4 * j4);
-            float4 s = *p;
-            const float m = s_max[i];
-            const int j = 4 * j4;
-            s.x = j + 0 < lim ? exp_rn(__fsub_rn(s.x, m)) : 0.0f;
-            s.y = j + 1 < lim ? exp_rn(__fsub_rn(s.y, m)) : 0.0f;
-            s.z = j + 2 < lim ? exp_rn(__fsub_rn(s.z, m)) : 0.0f;
-            s.w = j + 3 < lim ? exp_rn(__fsub_rn(s.w, m)) : 0.0f;
-            *p = s;
-        }
-        __syncthreads();
-        if (tid < kAttRows) {
-            // the denominator: one thread per row, keys in ascending order
-            const int i = tid;
-            const int lim = i < rows ? (a.causal ? min(kend, i0 + i + 1) : kend) : 0;
-            const int l4 = (lim + 3) / 4;       // entries past lim are 0: adding them changes nothing
-            float d = 0.0f;
-            for (int j4 = 0; j4 < l4; ++j4) {
-                const float4 e = *reinterpret_cast<const float4*>(ss + i * sp + 4 * j4);
-                d = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(d, e.x), e.y), e.z), e.w);
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1) {
+                ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+                mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
             }
-            s_rinv[i] = lim > 0 ? __frcp_rn(d) : 0.0f;
+            if (part == 0) {
+                s_max[il] = ml;
+                s_max[ih] = mh;
+            }
         }
         __syncthreads();
-        for (int e = tid; e < kAttRows * (kpad / 4); e += kAttThreads) {
-            const int i = e / (kpad / 4), j4 = e % (kpad / 4);
-            float4* p = reinterpret_cast<float4*>(ss + i * sp + 4 * j4);
-            float4 w = *p;
-            const float r = s_rinv[i];
-            w.x = __fmul_rn(w.x, r);
-            w.y = __fmul_rn(w.y, r);
-            w.z = __fmul_rn(w.z, r);
-            w.w = __fmul_rn(w.w, r);
-            *p = w;
+        // exponentials, keys at or past a row's limit set to exactly 0
+        for (int e = tid; e < (kAttRows / 2) * (kpad / 2); e += kAttThreads) {
+            const int pid = e / (kpad / 2), j = 2 * (e % (kpad / 2));
+            const int il = pair_row(pid, 0), ih = il + 8;
+            const int ll = row_lim(il), lh = row_lim(ih);
+            const float ml = s_max[il], mh = s_max[ih];
+            float4* p = reinterpret_cast<float4*>(ss + pid * sp + 2 * j);
+            float4 v = *p;                      // (j, lo) (j, hi) (j + 1, lo) (j + 1, hi)
+            v.x = j < ll ? exp_rn(__fsub_rn(v.x, ml)) : 0.0f;
+            v.y = j < lh ? exp_rn(__fsub_rn(v.y, mh)) : 0.0f;
+            v.z = j + 1 < ll ? exp_rn(__fsub_rn(v.z, ml)) : 0.0f;
+            v.w = j + 1 < lh ? exp_rn(__fsub_rn(v.w, mh)) : 0.0f;
+            *p = v;
+        }
+        __syncthreads();
+        if (tid < kAttRows / 2) {
+            // the denominators: one thread per row pair, each row's keys in ascending order
+            const int pid = tid, il = pair_row(pid, 0), ih = il + 8;
+            const int lim = max(row_lim(il), row_lim(ih));  // entries past a row's own limit are 0
+            float dl = 0.0f, dh = 0.0f;
+            for (int j = 0; j < lim; j += 2) {
+                const float4 v = *reinterpret_cast<const float4*>(ss + pid * sp + 2 * j);
+                dl = __fadd_rn(__fadd_rn(dl, v.x), v.z);
+                dh = __fadd_rn(__fadd_rn(dh, v.y), v.w);
+            }
+            s_rinv[il] = row_lim(il) > 0 ? __frcp_rn(dl) : 0.0f;
+            s_rinv[ih] = row_lim(ih) > 0 ? __frcp_rn(dh) : 0.0f;
+        }
+        __syncthreads();
+        for (int e = tid; e < (kAttRows / 2) * (kpad / 2); e += kAttThreads) {
+            const int pid = e / (kpad / 2), j = 2 * (e % (kpad / 2));
+            const int il = pair_row(pid, 0);
+            const float rl = s_rinv[il], rh = s_rinv[il + 8];
+            float4* p = reinterpret_cast<float4*>(ss + pid * sp + 2 * j);
+            float4 v = *p;
+            v.x = __fmul_rn(v.x, rl);
+            v.y = __fmul_rn(v.y, rh);
+            v.z = __fmul_rn(v.z, rl);
+            v.w = __fmul_rn(v.w, rh);
+            *p = v;
         }
 
         // ---- attended[i][t] = sum_j w[i][j] * v[j][t], j ascending
-        float o[8][NC][4];
+        uint64_t O[4][NC][4];                   // {o[i][t + c], o[i + 8][t + c]}
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
+        for (int rp = 0; rp < 4; ++rp)
 #pragma unroll
             for (int g = 0; g < NC; ++g)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) o[r][g][c] = 0.0f;
+                for (int c = 0; c < 4; ++c) O[rp][g][c] = 0ull;
         for (int kt = 0; kt < ntiles; ++kt) {
             __syncthreads();                    // weights final / ks free
             pre.store(ks);
@@ -260,10 +342,14 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
             if (kt + 1 < ntiles) pre.load(vg, a.v_rs, (kt + 1) * kAttKeys, kend);
 #pragma unroll 2
             for (int j4 = 0; j4 < kAttKeys / 4; ++j4) {
-                float4 wv[8];
+                const int j = kt * kAttKeys + 4 * j4;
+                float4 wa[4], wb[4];
 #pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    wv[r] = *reinterpret_cast<const float4*>(ss + (ty + 8 * r) * sp + kt * kAttKeys + 4 * j4);
+                for (int rp = 0; rp < 4; ++rp) {
+                    const float* w = ss + (ty + 8 * rp) * sp + 2 * j;
+                    wa[rp] = *reinterpret_cast<const float4*>(w);       // keys j, j + 1
+                    wb[rp] = *reinterpret_cast<const float4*>(w + 4);   // keys j + 2, j + 3
+                }
 #pragma unroll
                 for (int g = 0; g < NC; ++g) {
                     const int t = 4 * tx + 64 * g;
@@ -271,17 +357,21 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
                         float4 vv[4];
 #pragma unroll
                         for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4*>(ks + (4 * j4 + u) * P + t);
-#pragma unroll
-                        for (int r = 0; r < 8; ++r) {
-                            const float wr[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                o[r][g][0] = __fadd_rn(o[r][g][0], __fmul_rn(wr[u], vv[u].x));
-                                o[r][g][1] = __fadd_rn(o[r][g][1], __fmul_rn(wr[u], vv[u].y));
-                                o[r][g][2] = __fadd_rn(o[r][g][2], __fmul_rn(wr[u], vv[u].z));
-                                o[r][g][3] = __fadd_rn(o[r][g][3], __fmul_rn(wr[u], vv[u].w));
-                            }
+#define KZ_PV_STEP(WV, LO, HI, U)                                                         \
+                        {                                                                 \
+                            const uint64_t vd[4] = {pk(vv[U].x, vv[U].x), pk(vv[U].y, vv[U].y), \
+                                                    pk(vv[U].z, vv[U].z), pk(vv[U].w, vv[U].w)}; \
+                            _Pragma("unroll") for (int rp = 0; rp < 4; ++rp) {            \
+                                const uint64_t wp = pk(WV[rp].LO, WV[rp].HI);             \
+                                _Pragma("unroll") for (int c = 0; c < 4; ++c)             \
+                                    mul_add2(O[rp][g][c], wp, vd[c]);                     \
+                            }                                                             \
                         }
+                        KZ_PV_STEP(wa, x, y, 0)
+                        KZ_PV_STEP(wa, z, w, 1)
+                        KZ_PV_STEP(wb, x, y, 2)
+                        KZ_PV_STEP(wb, z, w, 3)
+#undef KZ_PV_STEP
                     }
                 }
             }
@@ -289,17 +379,25 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
         // ---- head-merged output and its absmax
         float* og = a.out + (int64_t)b * a.seq_q * a.o_rs + (int64_t)h * DK;
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const int i = ty + 8 * r;
-            if (i < rows) {
+        for (int rp = 0; rp < 4; ++rp) {
+            const int il = pair_row(ty + 8 * rp, 0);
 #pragma unroll
-                for (int g = 0; g < NC; ++g) {
-                    const int t = 4 * tx + 64 * g;
-                    if (t < DK) {
-                        const float4 val = make_float4(o[r][g][0], o[r][g][1], o[r][g][2], o[r][g][3]);
-                        *reinterpret_cast<float4*>(og + (int64_t)(i0 + i) * a.o_rs + t) = val;
-                        amax = max(amax, max(max(abs_bits_f(val.x), abs_bits_f(val.y)),
-                                             max(abs_bits_f(val.z), abs_bits_f(val.w))));
+            for (int g = 0; g < NC; ++g) {
+                const int t = 4 * tx + 64 * g;
+                if (t < DK) {
+                    float lo[4], hi[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) upk(O[rp][g][c], lo[c], hi[c]);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int i = il + 8 * half;
+                        if (i < rows) {
+                            const float* o = half ? hi : lo;
+                            const float4 val = make_float4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<float4*>(og + (int64_t)(i0 + i) * a.o_rs + t) = val;
+                            amax = max(amax, max(max(abs_bits_f(val.x), abs_bits_f(val.y)),
+                                                 max(abs_bits_f(val.z), abs_bits_f(val.w))));
+                        }
                     }
                 }
             }
@@ -340,7 +438,8 @@ using namespace kz;
 extern "C" int kz_attention_smem_bytes(int64_t seq_k, int64_t d_k) {
     if (seq_k <= 0 || d_k <= 0 || d_k > kAttMaxDk) return 0;
     const int64_t kpad = (seq_k + kAttKeys - 1) / kAttKeys * kAttKeys;
-    const int64_t bytes = (int64_t)sizeof(float) * (2 * 64 * (d_k + 4) + kAttRows * (kpad + 4));
+    // query row pairs [32][2 d_k + 4], one K / V tile [64][d_k + 4], score row pairs [32][2 kpad + 4]
+    const int64_t bytes = (int64_t)sizeof(float) * (32 * (2 * d_k + 4) + 64 * (d_k + 4) + 32 * (2 * kpad + 4));
     return bytes <= (int64_t)kAttMaxSmem ? (int)bytes : 0;
 }
 
@@ -396,7 +495,7 @@ extern "C" int kz_attention_f32(const float* q, const float* k, const float* v, 
     a.d_k = (int)d_k;
     a.q_blocks = (int)((seq_q + kAttRows - 1) / kAttRows);
     a.items = (int)(batch * heads) * a.q_blocks;
-    a.s_pitch = (int)((seq_k + kAttKeys - 1) / kAttKeys * kAttKeys + 4);
+    a.s_pitch = (int)(2 * ((seq_k + kAttKeys - 1) / kAttKeys * kAttKeys) + 4);
     a.causal = causal ? 1 : 0;
     a.scale = scale;
     const int grid = (int)std::min<int64_t>(a.items, kAttMaxBlocks);
