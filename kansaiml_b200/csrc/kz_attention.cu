@@ -31,12 +31,12 @@
 // the block's whole score rows on chip, runs the softmax there and streams
 // 64-key tiles of V for the weighted sum.  Thread tile 8 query rows x 4 keys
 // (row pairs i, i + 8 with i = ty + 16 rp; keys tx + 16 c).  The arithmetic
-// runs on sm_100's packed f32x2 instructions, one instruction per two rows,
-// each half rounded as the scalar instruction would: query rows and score
-// rows are stored pair-interleaved so their 16-byte loads are the packed
-// operands, and per 4 reduction steps 12 shared loads feed 128 packed
-// instructions (256 fp32 operations).  The next tile's global loads are
-// issued into registers before the current tile's arithmetic.  The output is written
+// sums run on sm_100's packed f32x2 add, one instruction per two rows, each
+// half rounded as the scalar instruction would (the products are scalar
+// multiplies): query rows and score rows are stored pair-interleaved so their
+// 16-byte loads give both rows' operands, and per 4 reduction steps 12 shared
+// loads feed 192 instructions (256 fp32 operations).  The next tile's global
+// loads are issued into registers before the current tile's arithmetic.  The output is written
 // head-merged ([batch, seq_q, heads * d_k], the layout the output projection
 // reads) with the absmax partials of every value, so the projection's
 // per-tensor quantize needs no extra pass.
@@ -83,9 +83,12 @@ __device__ __forceinline__ float exp_rn(float x) {
     return x < -104.0f ? 0.0f : __double2float_rn(exp((double)x));
 }
 
-// Packed fp32 pairs: sm_100's f32x2 arithmetic rounds each half exactly like
-// the scalar instruction (round to nearest, subnormals kept), so a pair of
-// separately rounded products / sums costs one instruction instead of two.
+// Packed fp32 pairs: sm_100's f32x2 add rounds each half exactly like the
+// scalar instruction (round to nearest, subnormals kept), so two separately
+// rounded sums cost one instruction.  The products stay scalar multiplies: a
+// packed multiply whose only use is a packed add is fused into one packed FMA
+// by the code generator (single rounding, even with --fmad=false), while a
+// pair of scalar .rn products feeding the packed add is not.
 __device__ __forceinline__ uint64_t pk(float lo, float hi) {
     uint64_t r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -94,11 +97,10 @@ __device__ __forceinline__ uint64_t pk(float lo, float hi) {
 __device__ __forceinline__ void upk(uint64_t r, float& lo, float& hi) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
 }
-// d = d + a * b per half, the product rounded before the sum (no FMA)
-__device__ __forceinline__ void mul_add2(uint64_t& d, uint64_t a, uint64_t b) {
-    uint64_t p;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(a), "l"(b));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(d), "l"(p));
+// d = {d.lo + lo * b, d.hi + hi * b}, each product rounded before its sum
+__device__ __forceinline__ void mul_add2(uint64_t& d, float lo, float hi, float b) {
+    const float p0 = __fmul_rn(lo, b), p1 = __fmul_rn(hi, b);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(d), "l"(pk(p0, p1)));
 }
 
 // Row pairs.  Query rows i and i + 8 (i = ty + 16 rp) are one pair, id
@@ -170,11 +172,9 @@ __device__ __forceinline__ void score_tile(const float* qp, const float* ks, int
 #pragma unroll
         for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (tx + 16 * c) * P + 4 * t4);
 #define KZ_QK_STEP(QV, LO, HI, KC)                                                   \
-        _Pragma("unroll") for (int c = 0; c < 4; ++c) {                              \
-            const uint64_t kd = pk(kv[c].KC, kv[c].KC);                              \
+        _Pragma("unroll") for (int c = 0; c < 4; ++c)                                \
             _Pragma("unroll") for (int rp = 0; rp < 4; ++rp)                         \
-                if (!DIAG || rp >= c) mul_add2(A[rp][c], pk(QV[rp].LO, QV[rp].HI), kd); \
-        }
+                if (!DIAG || rp >= c) mul_add2(A[rp][c], QV[rp].LO, QV[rp].HI, kv[c].KC);
         KZ_QK_STEP(qa, x, y, x)
         KZ_QK_STEP(qa, z, w, y)
         KZ_QK_STEP(qb, x, y, z)
@@ -358,14 +358,11 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
 #pragma unroll
                         for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4*>(ks + (4 * j4 + u) * P + t);
 #define KZ_PV_STEP(WV, LO, HI, U)                                                         \
-                        {                                                                 \
-                            const uint64_t vd[4] = {pk(vv[U].x, vv[U].x), pk(vv[U].y, vv[U].y), \
-                                                    pk(vv[U].z, vv[U].z), pk(vv[U].w, vv[U].w)}; \
-                            _Pragma("unroll") for (int rp = 0; rp < 4; ++rp) {            \
-                                const uint64_t wp = pk(WV[rp].LO, WV[rp].HI);             \
-                                _Pragma("unroll") for (int c = 0; c < 4; ++c)             \
-                                    mul_add2(O[rp][g][c], wp, vd[c]);                     \
-                            }                                                             \
+                        _Pragma("unroll") for (int rp = 0; rp < 4; ++rp) {                \
+                            mul_add2(O[rp][g][0], WV[rp].LO, WV[rp].HI, vv[U].x);         \
+                            mul_add2(O[rp][g][1], WV[rp].LO, WV[rp].HI, vv[U].y);         \
+                            mul_add2(O[rp][g][2], WV[rp].LO, WV[rp].HI, vv[U].z);         \
+                            mul_add2(O[rp][g][3], WV[rp].LO, WV[rp].HI, vv[U].w);         \
                         }
                         KZ_PV_STEP(wa, x, y, 0)
                         KZ_PV_STEP(wa, z, w, 1)
