@@ -29,13 +29,13 @@
 // then 64-key tiles of K, in shared memory (row pitch d_k + 4 floats, so the
 // 16-byte reads of 8 consecutive lanes fall in distinct bank groups), keeps
 // the block's whole score rows on chip, runs the softmax there and streams
-// 64-key tiles of V for the weighted sum.  Thread tile 8 query rows x 4 keys
-// (row pairs i, i + 8 with i = ty + 16 rp; keys tx + 16 c).  The arithmetic
+// 64-key tiles of V for the weighted sum.  256 threads, thread tile 4 query
+// rows x 4 keys (row pairs ty + 16 rp of rows i, i + 8; keys tx + 16 c).  The
 // sums run on sm_100's packed f32x2 add, one instruction per two rows, each
 // half rounded as the scalar instruction would (the products are scalar
 // multiplies): query rows and score rows are stored pair-interleaved so their
-// 16-byte loads give both rows' operands, and per 4 reduction steps 12 shared
-// loads feed 192 instructions (256 fp32 operations).  The next tile's global
+// 16-byte loads give both rows' operands, and per 4 reduction steps 8 shared
+// loads feed 96 instructions (128 fp32 operations).  The next tile's global
 // loads are issued into registers before the current tile's arithmetic.  The output is written
 // head-merged ([batch, seq_q, heads * d_k], the layout the output projection
 // reads) with the absmax partials of every value, so the projection's
@@ -52,7 +52,7 @@ namespace {
 
 constexpr int kAttRows = 64;      // query rows per CTA
 constexpr int kAttKeys = 64;      // keys per staged K / V tile
-constexpr int kAttThreads = 128;  // 8 x 16 threads
+constexpr int kAttThreads = 256;  // 16 x 16 threads
 constexpr int kAttMaxDk = 128;
 constexpr int kAttMaxBlocks = KZ_PARTIALS_WORDS - 3;
 // opt-in dynamic shared memory ceiling: 227 KB per CTA less room for the
@@ -103,8 +103,8 @@ __device__ __forceinline__ void mul_add2(uint64_t& d, float lo, float hi, float 
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(d), "l"(pk(p0, p1)));
 }
 
-// Row pairs.  Query rows i and i + 8 (i = ty + 16 rp) are one pair, id
-// pid = ty + 8 rp; the pair's values are interleaved in shared memory
+// Row pairs.  Query rows i and i + 8 (i = 16 g + o, o < 8) are one pair, id
+// pid = o + 8 g; the pair's values are interleaved in shared memory
 // (element (i, x) at pair[2 x + (i / 8) % 2]) so one 16-byte load yields the
 // two rows' values at two consecutive x -- ready-made f32x2 operands.
 __device__ __forceinline__ int pair_id(int i) { return (i & 7) + 8 * (i >> 4); }
@@ -154,18 +154,20 @@ struct TileRegs {
 };
 
 // A[rp][c] = {s[i][j], s[i + 8][j]} += q[.][t] * k[j][t] for t ascending
-// (i = ty + 16 rp, j = tx + 16 c of the tile), each product and sum rounded
-// on its own.  DIAG (causal diagonal tile) skips the pairs rp < c, whose rows
-// all precede their keys.
+// (row pair ty + 16 rp, whose rows lie in the 16-row group 2 rp + ty / 8;
+// key j = tx + 16 c of the tile), each product and sum rounded on its own.
+// DIAG (causal diagonal tile) skips the pairs whose row group precedes the
+// key group (every row before every key; the test is uniform per warp).
 template <int DK, bool DIAG>
-__device__ __forceinline__ void score_tile(const float* qp, const float* ks, int ty, int tx, uint64_t (&A)[4][4]) {
+__device__ __forceinline__ void score_tile(const float* qp, const float* ks, int ty, int tx, uint64_t (&A)[2][4]) {
     constexpr int P = DK + 4, PQ = 2 * DK + 4;
+    const int hb = ty >> 3;
 #pragma unroll 2
     for (int t4 = 0; t4 < DK / 4; ++t4) {
-        float4 qa[4], qb[4], kv[4];
+        float4 qa[2], qb[2], kv[4];
 #pragma unroll
-        for (int rp = 0; rp < 4; ++rp) {
-            const float* row = qp + (ty + 8 * rp) * PQ + 8 * t4;
+        for (int rp = 0; rp < 2; ++rp) {
+            const float* row = qp + (ty + 16 * rp) * PQ + 8 * t4;
             qa[rp] = *reinterpret_cast<const float4*>(row);        // t, t + 1
             qb[rp] = *reinterpret_cast<const float4*>(row + 4);    // t + 2, t + 3
         }
@@ -173,8 +175,8 @@ __device__ __forceinline__ void score_tile(const float* qp, const float* ks, int
         for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (tx + 16 * c) * P + 4 * t4);
 #define KZ_QK_STEP(QV, LO, HI, KC)                                                   \
         _Pragma("unroll") for (int c = 0; c < 4; ++c)                                \
-            _Pragma("unroll") for (int rp = 0; rp < 4; ++rp)                         \
-                if (!DIAG || rp >= c) mul_add2(A[rp][c], QV[rp].LO, QV[rp].HI, kv[c].KC);
+            _Pragma("unroll") for (int rp = 0; rp < 2; ++rp)                         \
+                if (!DIAG || 2 * rp + hb >= c) mul_add2(A[rp][c], QV[rp].LO, QV[rp].HI, kv[c].KC);
         KZ_QK_STEP(qa, x, y, x)
         KZ_QK_STEP(qa, z, w, y)
         KZ_QK_STEP(qb, x, y, z)
@@ -184,7 +186,7 @@ __device__ __forceinline__ void score_tile(const float* qp, const float* ks, int
 }
 
 template <int DK>
-__global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a) {
+__global__ void __launch_bounds__(kAttThreads, DK <= 64 ? 2 : 1) attention_ref_kernel(AttArgs a) {
     constexpr int P = DK + 4;                   // K / V tile pitch
     constexpr int PQ = 2 * DK + 4;              // Q row-pair pitch
     constexpr int NC = (DK + 63) / 64;          // output column groups per thread
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
     griddep_launch_dependents();
     griddep_wait();
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;     // keys tx + 16c, row pairs ty + 8rp
+    const int tx = tid & 15, ty = tid >> 4;     // keys tx + 16c, row pairs ty + 16rp
     const int sp = a.s_pitch;                   // floats per row pair: 2 x keys + 4
     uint32_t amax = 0;
 
@@ -231,9 +233,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
             pre.store(ks);
             __syncthreads();
             if (kt + 1 < ntiles) pre.load(kg, a.k_rs, (kt + 1) * kAttKeys, kend);
-            uint64_t A[4][4];
+            uint64_t A[2][4];
 #pragma unroll
-            for (int rp = 0; rp < 4; ++rp)
+            for (int rp = 0; rp < 2; ++rp)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) A[rp][c] = 0ull;    // +0.0f, +0.0f
             if (a.causal && kt == ntiles - 1)
@@ -241,8 +243,8 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
             else
                 score_tile<DK, false>(qp, ks, ty, tx, A);
 #pragma unroll
-            for (int rp = 0; rp < 4; ++rp) {
-                const int pid = ty + 8 * rp, il = pair_row(pid, 0), ih = il + 8;
+            for (int rp = 0; rp < 2; ++rp) {
+                const int pid = ty + 16 * rp, il = pair_row(pid, 0), ih = il + 8;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int j = kt * kAttKeys + tx + 16 * c;
@@ -264,18 +266,18 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
 
         // ---- softmax of each row over its keys [0, lim): max, exp(s - max), ordered sum, * 1/sum
         {
-            // row-pair max, four threads per pair (order-free)
-            const int pid = tid >> 2, part = tid & 3;
+            // row-pair max, eight threads per pair (order-free)
+            const int pid = tid >> 3, part = tid & 7;
             const int il = pair_row(pid, 0), ih = il + 8;
             const int ll = row_lim(il), lh = row_lim(ih);
             float ml = -INFINITY, mh = -INFINITY;
-            for (int j = part; j < max(ll, lh); j += 4) {
+            for (int j = part; j < max(ll, lh); j += 8) {
                 const float2 v = *reinterpret_cast<const float2*>(ss + pid * sp + 2 * j);
                 if (j < ll) ml = fmaxf(ml, v.x);
                 if (j < lh) mh = fmaxf(mh, v.y);
             }
 #pragma unroll
-            for (int o = 1; o <= 2; o <<= 1) {
+            for (int o = 1; o <= 4; o <<= 1) {
                 ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
                 mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
             }
@@ -328,9 +330,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
         }
 
         // ---- attended[i][t] = sum_j w[i][j] * v[j][t], j ascending
-        uint64_t O[4][NC][4];                   // {o[i][t + c], o[i + 8][t + c]}
+        uint64_t O[2][NC][4];                   // {o[i][t + c], o[i + 8][t + c]}
 #pragma unroll
-        for (int rp = 0; rp < 4; ++rp)
+        for (int rp = 0; rp < 2; ++rp)
 #pragma unroll
             for (int g = 0; g < NC; ++g)
 #pragma unroll
@@ -343,10 +345,10 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
 #pragma unroll 2
             for (int j4 = 0; j4 < kAttKeys / 4; ++j4) {
                 const int j = kt * kAttKeys + 4 * j4;
-                float4 wa[4], wb[4];
+                float4 wa[2], wb[2];
 #pragma unroll
-                for (int rp = 0; rp < 4; ++rp) {
-                    const float* w = ss + (ty + 8 * rp) * sp + 2 * j;
+                for (int rp = 0; rp < 2; ++rp) {
+                    const float* w = ss + (ty + 16 * rp) * sp + 2 * j;
                     wa[rp] = *reinterpret_cast<const float4*>(w);       // keys j, j + 1
                     wb[rp] = *reinterpret_cast<const float4*>(w + 4);   // keys j + 2, j + 3
                 }
@@ -358,7 +360,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
 #pragma unroll
                         for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4*>(ks + (4 * j4 + u) * P + t);
 #define KZ_PV_STEP(WV, LO, HI, U)                                                         \
-                        _Pragma("unroll") for (int rp = 0; rp < 4; ++rp) {                \
+                        _Pragma("unroll") for (int rp = 0; rp < 2; ++rp) {                \
                             mul_add2(O[rp][g][0], WV[rp].LO, WV[rp].HI, vv[U].x);         \
                             mul_add2(O[rp][g][1], WV[rp].LO, WV[rp].HI, vv[U].y);         \
                             mul_add2(O[rp][g][2], WV[rp].LO, WV[rp].HI, vv[U].z);         \
@@ -376,8 +378,8 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_ref_kernel(AttArgs a
         // ---- head-merged output and its absmax
         float* og = a.out + (int64_t)b * a.seq_q * a.o_rs + (int64_t)h * DK;
 #pragma unroll
-        for (int rp = 0; rp < 4; ++rp) {
-            const int il = pair_row(ty + 8 * rp, 0);
+        for (int rp = 0; rp < 2; ++rp) {
+            const int il = pair_row(ty + 16 * rp, 0);
 #pragma unroll
             for (int g = 0; g < NC; ++g) {
                 const int t = 4 * tx + 64 * g;
