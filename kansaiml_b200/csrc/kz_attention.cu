@@ -185,6 +185,43 @@ __device__ __forceinline__ void score_tile(const float* qp, const float* ks, int
     }
 }
 
+// O[rp][g][c] = {o[i][t + c], o[i + 8][t + c]} += w[.][j + u] * v[j + u][t + c]
+// for u = 0..3 (row pairs ty + 16 rp with rp >= RP0; t = 4 tx + 64 g), each
+// product and sum rounded on its own, keys in ascending order.
+template <int DK, int RP0>
+__device__ __forceinline__ void pv_step(const float* ss, const float* ks, int sp, int ty, int tx, int j, int j4,
+                                        uint64_t (&O)[2][(DK + 63) / 64][4]) {
+    constexpr int P = DK + 4, NC = (DK + 63) / 64;
+    float4 wa[2], wb[2];
+#pragma unroll
+    for (int rp = RP0; rp < 2; ++rp) {
+        const float* w = ss + (ty + 16 * rp) * sp + 2 * j;
+        wa[rp] = *reinterpret_cast<const float4*>(w);       // keys j, j + 1
+        wb[rp] = *reinterpret_cast<const float4*>(w + 4);   // keys j + 2, j + 3
+    }
+#pragma unroll
+    for (int g = 0; g < NC; ++g) {
+        const int t = 4 * tx + 64 * g;
+        if (t < DK) {
+            float4 vv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4*>(ks + (4 * j4 + u) * P + t);
+#define KZ_PV_STEP(WV, LO, HI, U)                                             \
+            _Pragma("unroll") for (int rp = RP0; rp < 2; ++rp) {              \
+                mul_add2(O[rp][g][0], WV[rp].LO, WV[rp].HI, vv[U].x);         \
+                mul_add2(O[rp][g][1], WV[rp].LO, WV[rp].HI, vv[U].y);         \
+                mul_add2(O[rp][g][2], WV[rp].LO, WV[rp].HI, vv[U].z);         \
+                mul_add2(O[rp][g][3], WV[rp].LO, WV[rp].HI, vv[U].w);         \
+            }
+            KZ_PV_STEP(wa, x, y, 0)
+            KZ_PV_STEP(wa, z, w, 1)
+            KZ_PV_STEP(wb, x, y, 2)
+            KZ_PV_STEP(wb, z, w, 3)
+#undef KZ_PV_STEP
+        }
+    }
+}
+
 template <int DK>
 __global__ void __launch_bounds__(kAttThreads, DK <= 64 ? 2 : 1) attention_ref_kernel(AttArgs a) {
     constexpr int P = DK + 4;                   // K / V tile pitch
@@ -342,37 +379,19 @@ __global__ void __launch_bounds__(kAttThreads, DK <= 64 ? 2 : 1) attention_ref_k
             pre.store(ks);
             __syncthreads();
             if (kt + 1 < ntiles) pre.load(vg, a.v_rs, (kt + 1) * kAttKeys, kend);
+            // causal diagonal tile: key segment s (keys 16 s .. 16 s + 15) needs
+            // only the row groups g >= s (g = 2 rp + ty / 8); the pairs of an
+            // earlier group have weight 0 there (keys after the row), and
+            // adding their +-0 products would change no sum
+            const bool diag = a.causal && kt == ntiles - 1;
 #pragma unroll 2
             for (int j4 = 0; j4 < kAttKeys / 4; ++j4) {
                 const int j = kt * kAttKeys + 4 * j4;
-                float4 wa[2], wb[2];
-#pragma unroll
-                for (int rp = 0; rp < 2; ++rp) {
-                    const float* w = ss + (ty + 16 * rp) * sp + 2 * j;
-                    wa[rp] = *reinterpret_cast<const float4*>(w);       // keys j, j + 1
-                    wb[rp] = *reinterpret_cast<const float4*>(w + 4);   // keys j + 2, j + 3
-                }
-#pragma unroll
-                for (int g = 0; g < NC; ++g) {
-                    const int t = 4 * tx + 64 * g;
-                    if (t < DK) {
-                        float4 vv[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4*>(ks + (4 * j4 + u) * P + t);
-#define KZ_PV_STEP(WV, LO, HI, U)                                                         \
-                        _Pragma("unroll") for (int rp = 0; rp < 2; ++rp) {                \
-                            mul_add2(O[rp][g][0], WV[rp].LO, WV[rp].HI, vv[U].x);         \
-                            mul_add2(O[rp][g][1], WV[rp].LO, WV[rp].HI, vv[U].y);         \
-                            mul_add2(O[rp][g][2], WV[rp].LO, WV[rp].HI, vv[U].z);         \
-                            mul_add2(O[rp][g][3], WV[rp].LO, WV[rp].HI, vv[U].w);         \
-                        }
-                        KZ_PV_STEP(wa, x, y, 0)
-                        KZ_PV_STEP(wa, z, w, 1)
-                        KZ_PV_STEP(wb, x, y, 2)
-                        KZ_PV_STEP(wb, z, w, 3)
-#undef KZ_PV_STEP
-                    }
-                }
+                const int rp0 = diag ? max(0, ((j4 >> 2) - (ty >> 3) + 1) >> 1) : 0;   // uniform per warp
+                if (rp0 == 0)
+                    pv_step<DK, 0>(ss, ks, sp, ty, tx, j, j4, O);
+                else if (rp0 == 1)
+                    pv_step<DK, 1>(ss, ks, sp, ty, tx, j, j4, O);
             }
         }
         // ---- head-merged output and its absmax
