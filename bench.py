@@ -1166,7 +1166,8 @@ def run_transformer(args, rank, world, local_rank, dev):
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": "config3: int8 2-layer decoder d256 h4 ff1024 vocab65 ctx256, batch 32",
                    "global_batch": tokens, "seq_len": 256, "parallelism": "single GPU",
-                   "launch": f"CUDA graphs of {reps} forwards replayed back to back"},
+                   "launch": f"CUDA graphs of {reps} forwards replayed back to back",
+                   "attention": "kz_attention_f32: the reference's operation order, fp32, no FMA"},
         "int8_ops_per_step": ops, "int8_tops": ops / (ms / 1e3) / 1e12,
         "clocks": clocks,
     }
