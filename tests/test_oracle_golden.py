@@ -11,6 +11,7 @@ import pytest
 import inputs
 from conftest import golden
 from oracle import cpu as ocpu
+from oracle import refpkg
 
 
 @pytest.fixture(scope="module")
@@ -311,3 +312,36 @@ def test_oracle_qlinear_w8a32_is_the_k_ordered_loop(M, N, K, relu, seed):
             v = np.float32(acc + bias[j])
             ref[i, j] = (v if v > 0 else np.float32(0.0)) if relu else v   # x > 0 ? x : 0, as Ops.cpp
     assert y.tobytes() == ref.tobytes()
+
+
+@pytest.mark.skipif(not refpkg.reference_available(), reason="reference checkout / compiled core not present")
+def test_attention_oracle_vs_reference_random_shapes():
+    """Beyond the fixtures: random shapes (1-3 batches, 1-4 heads, head widths
+    8 / 16 / 32, query and key lengths 1-90), the reference's own
+    MultiHeadAttention.forward with identity projections against the oracle
+    with the host's expf -- bit for bit -- with and without a random additive
+    mask."""
+    kansai = refpkg.import_reference_kansai()
+    from kansai_reference import nn
+    core = kansai.core
+
+    def from_np(x):
+        return core.from_flat(np.asarray(x, np.float32).ravel().tolist(), list(x.shape))
+
+    rs = np.random.RandomState(77)
+    for case in range(12):
+        B, H, dk = rs.randint(1, 4), rs.randint(1, 5), int(rs.choice([8, 16, 32]))
+        Sq, Sk = rs.randint(1, 91), rs.randint(1, 91)
+        D = H * dk
+        q = (rs.standard_normal((B, Sq, D)) * 2).astype(np.float32)
+        k = (rs.standard_normal((B, Sk, D)) * 2).astype(np.float32)
+        v = rs.standard_normal((B, Sk, D)).astype(np.float32)
+        mask = None
+        if case % 2:
+            mask = (rs.uniform(-5, 0, (B, 1, Sq, Sk)) * (rs.uniform(size=(B, 1, Sq, Sk)) < 0.5)).astype(np.float32)
+        mha = nn.MultiHeadAttention(D, H)
+        eye = from_np(np.eye(D, dtype=np.float32))
+        mha.w_q = mha.w_k = mha.w_v = mha.w_o = eye
+        y = mha.forward(from_np(q), from_np(k), from_np(v), mask=from_np(mask) if mask is not None else None)
+        ref = np.asarray(y.tolist(), np.float32).reshape(B, Sq, D)
+        assert ocpu.attention(q, k, v, H, mask=mask, exp="libm").tobytes() == ref.tobytes(), (case, B, H, dk, Sq, Sk)
