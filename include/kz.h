@@ -196,6 +196,11 @@ int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double
 /* out[i] = (float)((double)q[i] * scale): quantize.py:76 in double, narrowed
  * to fp32 as Tensor::from_flat does (core/src/Tensor.cpp:94-100). */
 int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, kz_stream_t stream);
+/* Which exact form kz_dequantize_i8_f32 takes for `scale` (host-only, no
+ * device call): 0 the table-free split form (fp32 fma(q, s_hi, q * s_lo),
+ * which equals (float)((double)q * scale) for every byte at this scale), 1
+ * the shared-memory table of the 256 values (any other scale; rare). */
+int kz_dequantize_uses_table(double scale);
 
 /* Inverse of kz_quantize_cols_f32: out[K, N] (reference layout) from qT[N, K]
  * and per-channel double scales (device pointer). */

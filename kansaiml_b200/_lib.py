@@ -47,6 +47,7 @@ SIGNATURES = {
     "kz_quantize_cols_f32_noalloc": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "kz_quantize_rows_f32": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "kz_dequantize_i8_f32": (_I, [_P, _I64, _D, _P, _P]),
+    "kz_dequantize_uses_table": (_I, [_D]),
     "kz_dequantize_cols_i8_f32": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "kz_qlinear_w8a32_f32": (_I, [_P, _I64, _I64, _P, _D, _P, _I64, _I, _P, _P]),
     "kz_set_sm_count_target": (_I, [_I]),

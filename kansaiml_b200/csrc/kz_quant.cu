@@ -39,6 +39,9 @@
 #include <cfloat>
 #include <mutex>
 
+#include <cmath>
+#include <cstring>
+
 #include "kz_common.cuh"
 
 namespace kz {
@@ -913,7 +916,17 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 
 // -------------------------------------------------------------- dequantize
 
-// Per-tensor dequantize through a lookup table: entry u holds
+// Per-tensor dequantize, two exact forms.  The value of a code q is
+// (float)((double)q * scale) (quantize.py:76-77, from_flat).  Form 1 (no
+// table): with s_hi = (float)scale and s_lo = (float)(scale - s_hi),
+// fma(q, s_hi, q * s_lo) in fp32 is within about 2^-47 of q * scale and so
+// rounds to the same fp32 value for almost every scale; the host checks all
+// 256 byte values for the call's scale (dequant_split_exact) and takes this
+// form only when every one matches bit for bit.  Each code then costs a byte
+// permute that places it in the mantissa of 2^23 (offset binary), one exact
+// subtraction, one multiply and one FMA -- no shared memory and no per-block
+// set-up.  Form 2 (any other scale):
+// a lookup table: entry u holds
 // (float)((double)q * scale) for the code q whose byte is u -- every value the
 // reference can produce, indexed by the raw byte so that a lookup costs one
 // byte permute, one address computation and one shared load -- so
@@ -968,6 +981,46 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const int8_t* __restric
         for (int64_t j = (n4 << 2) + tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
     } else {
         for (int64_t j = tid; j < n; j += nthreads) out[j] = lut((uint8_t)q[j]);
+    }
+}
+
+// Form 1 (see above): thread t turns one word of four codes into one 16-byte
+// store; kDeqBatch words in flight per thread.
+__global__ void __launch_bounds__(256) dequantize_split_kernel(const int8_t* __restrict__ q, int64_t n, float s_hi,
+                                                               float s_lo, float* __restrict__ out) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    // byte k of wx (the code + 128) as the mantissa of 2^23: 2^23 + q + 128 exactly
+    auto val = [&](uint32_t wx, int k) {
+        const float f = __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7440u | (uint32_t)k));
+        const float qf = __fsub_rn(f, 8388736.0f);
+        return __fmaf_rn(qf, s_hi, __fmul_rn(qf, s_lo));
+    };
+    auto val1 = [&](int8_t c) {
+        const float qf = (float)(int)c;
+        return __fmaf_rn(qf, s_hi, __fmul_rn(qf, s_lo));
+    };
+    const bool aligned = (reinterpret_cast<uintptr_t>(q) & 3u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    if (aligned) {
+        const int64_t n4 = n >> 2;
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
+        float4* ov = reinterpret_cast<float4*>(out);
+        for (int64_t i0 = tid; i0 < n4; i0 += kDeqBatch * nthreads) {
+            uint32_t w[kDeqBatch];
+#pragma unroll
+            for (int u = 0; u < kDeqBatch; ++u) {
+                const int64_t i = i0 + u * nthreads;
+                w[u] = i < n4 ? __ldcs(qw + i) ^ 0x80808080u : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < kDeqBatch; ++u) {
+                const int64_t i = i0 + u * nthreads;
+                if (i < n4) __stcs(ov + i, make_float4(val(w[u], 0), val(w[u], 1), val(w[u], 2), val(w[u], 3)));
+            }
+        }
+        for (int64_t j = (n4 << 2) + tid; j < n; j += nthreads) out[j] = val1(q[j]);
+    } else {
+        for (int64_t j = tid; j < n; j += nthreads) out[j] = val1(q[j]);
     }
 }
 
@@ -1261,6 +1314,33 @@ int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double
     return launch_status("quantize_rows_kernel");
 }
 
+// True when fma(q, s_hi, q * s_lo) in fp32 equals (float)((double)q * scale)
+// for all 256 byte values q (the split form of the device kernel; the host's
+// fmaf and multiply are IEEE operations like the device's).
+static bool dequant_split_exact(double scale, float* s_hi, float* s_lo) {
+    const float hi = (float)scale;
+    const float lo = (float)(scale - (double)hi);
+    if (!std::isfinite(hi) || !std::isfinite(lo)) return false;
+    for (int c = -128; c <= 127; ++c) {
+        const float exact = (float)((double)c * scale);
+        const float qf = (float)c;
+        volatile float p = qf * lo;            // rounded on its own, as on the device
+        const float cand = std::fma(qf, hi, (float)p);
+        uint32_t a, b;
+        std::memcpy(&a, &exact, 4);
+        std::memcpy(&b, &cand, 4);
+        if (a != b) return false;
+    }
+    *s_hi = hi;
+    *s_lo = lo;
+    return true;
+}
+
+int kz_dequantize_uses_table(double scale) {
+    float hi, lo;
+    return dequant_split_exact(scale, &hi, &lo) ? 0 : 1;
+}
+
 int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, kz_stream_t stream) {
     KZ_REQUIRE(n >= 0, "kz_dequantize_i8_f32: n must be >= 0");
     if (n == 0) return KZ_OK;
@@ -1268,8 +1348,16 @@ int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, k
     int st = check_device();
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    // up to six resident blocks per SM (each builds its own 33 KB table once)
     const int64_t per_block = 256 * 4 * kDeqBatch;
+    float s_hi, s_lo;
+    if (dequant_split_exact(scale, &s_hi, &s_lo)) {
+        // no shared memory: eight resident 256-thread blocks per SM
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + per_block - 1) / per_block,
+                                                                     8 * (int64_t)sm_count()));
+        dequantize_split_kernel<<<grid, 256, 0, s>>>(q, n, s_hi, s_lo, out);
+        return launch_status("dequantize_split_kernel");
+    }
+    // up to six resident blocks per SM (each builds its own 33 KB table once)
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + per_block - 1) / per_block, 6 * (int64_t)sm_count()));
     dequantize_kernel<<<grid, 256, 0, s>>>(q, n, scale, out);
     return launch_status("dequantize_kernel");

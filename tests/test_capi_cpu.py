@@ -76,6 +76,28 @@ def test_workspace_size_query():
     assert lib.kz_quantize_cols_workspace_bytes(16, 0) == 0
 
 
+def test_dequantize_form_query():
+    """The host picks the table-free dequantize only where the fp32 split
+    form equals (float)((double)q * scale) for every byte: checked here
+    against numpy for typical scales (split form) and for scales where it
+    cannot hold (subnormal products, a negative scale's -0.0, overflow, NaN)."""
+    import numpy as np
+    lib = _lib.load()
+    codes = np.arange(-128, 128).astype(np.float32)
+    rs = np.random.RandomState(4)
+    for s in [0.02 / 127, 1.0, 0.5, 1e-30] + list(rs.uniform(1e-5, 1.0, 200)):
+        assert lib.kz_dequantize_uses_table(float(s)) == 0, s
+        hi = np.float32(s)
+        lo = np.float32(np.float64(s) - np.float64(hi))
+        split = (codes.astype(np.float64) * np.float64(hi)       # exact: 24 x 24 bits
+                 + (codes * lo).astype(np.float32).astype(np.float64)).astype(np.float32)
+        exact = (codes.astype(np.float64) * s).astype(np.float32)
+        # the double sum above is exact or off by far less than a float ulp here
+        assert split.tobytes() == exact.tobytes(), s
+    for s in (3e-39, 1e-42, -0.5, 1e39, float("nan")):
+        assert lib.kz_dequantize_uses_table(s) == 1, s
+
+
 def test_exchange_entry_points_validate_arguments_without_gpu():
     """The overlapped-exchange entry points reject bad arguments before any
     device work, with a message."""

@@ -189,6 +189,29 @@ def test_dequantize_vs_oracle(kq, n):
     assert out.numpy().tobytes() == ocpu.dequantize(q, s).tobytes()
 
 
+@pytest.mark.parametrize("s", [0.02 / 127, 1.0, 3e-39, 2e-38, 1e-42, -0.5, 1e39])
+def test_dequantize_both_forms_bit_exact(kq, s):
+    """Every byte value (all 256, -128 included), aligned and at an odd
+    offset, at scales that take the table-free split form (0.02/127, 1.0) and
+    at scales that do not (subnormal products, a negative scale, one past fp32
+    range): the result equals (float)((double)q * scale) bit for bit either
+    way."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    assert lib.kz_dequantize_uses_table(s) == (0 if s in (0.02 / 127, 1.0) else 1)
+    codes = np.tile(np.arange(-128, 128, dtype=np.int16).astype(np.int8), 4099)
+    qd = torch.from_numpy(codes).cuda()
+    ref = (codes.astype(np.float64) * s).astype(np.float32)
+    for off in (0, 1):
+        n = codes.size - off
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        _lib.call("kz_dequantize_i8_f32", qd.data_ptr() + off, n, s, out.data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert out.cpu().numpy().tobytes() == ref[off:].tobytes(), (s, off)
+
+
 def test_dequantize_per_channel_roundtrip(kq):
     w = (np.random.RandomState(3).standard_normal((300, 200)) * 0.05).astype(np.float32)
     qt = kq.QTensor.from_tensor(dev(w), per_channel=True)
