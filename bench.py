@@ -79,10 +79,12 @@ def parse():
                     help="stack: pipelined NCCL all-gathers (collective, default), pipelined copy-engine pulls "
                          "(ce), copy-engine pulls feeding the gated GEMM (peer) or the all-gather inside the GEMM "
                          "launch (fused)")
-    ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp", "kernels", "gemm"],
+    ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp", "kernels", "gemm",
+                                           "attention", "dequantize"],
                     default="stack",
                     help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
-                         "mlp: config 1; kernels: the per-kernel entries alone; gemm: one GEMM shape (--shape)")
+                         "mlp: config 1; kernels: the per-kernel entries alone; gemm: one GEMM shape (--shape); "
+                         "attention / dequantize: that kernel alone at its bench shape (profiling targets)")
     ap.add_argument("--shape", default="8192,16384,16384", help="gemm workload: M,N,K")
     ap.add_argument("--tp", type=int, default=None,
                     help="stack: column-sharding group size (default: the stack's, N up to 4, else 4)")
@@ -1310,6 +1312,66 @@ def run_gemm(args, rank, world, local_rank, dev):
                           "tops": 2.0 * M * N * K / (us / 1e6) / 1e12, "launches": args.steps + max(args.warmup, 1)}))
 
 
+def run_attention(args, rank, world, local_rank, dev):
+    """Config 3's attention core alone (batch 32, 4 heads, 256 queries and
+    keys, d_k 64, causal, q|k|v read from one [32, 256, 768] projection
+    output): W + K launches, CUDA events around the K; a profiling target."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    B, S, D, H = 32, 256, 256, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(256)
+    qkv = torch.randn((B, S, 3 * D), generator=g, device=dev)
+    out = torch.empty((B, S, D), device=dev)
+    parts = torch.zeros(_lib.KZ_PARTIALS_WORDS, dtype=torch.int32, device=dev)
+
+    def call():
+        _ok(lib.kz_attention_f32(qkv.data_ptr(), qkv.data_ptr() + 4 * D, qkv.data_ptr() + 8 * D, B, H, S, S, D // H,
+                                 3 * D, 3 * D, 3 * D, None, 0, 0, 0, 1, 0.125, out.data_ptr(), D, parts.data_ptr(),
+                                 _sh(dev)))
+    _time_launches(args, rank, dev, call, "attention core, config 3 (32 x 4 heads x 256, d_k 64, causal)",
+                   {"op": B * H * (S * (S + 1) // 2) * 4.0 * (D // H)})
+
+
+def run_dequantize(args, rank, world, local_rank, dev):
+    """kz_dequantize_i8_f32 on config 2's 2048 x 4096 activation codes, scale
+    0.01: W + K launches, CUDA events around the K; a profiling target."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    n = M_TOK * K_IN
+    g = torch.Generator(device=dev)
+    g.manual_seed(n)
+    q = torch.randint(-127, 128, (n,), dtype=torch.int8, device=dev, generator=g)
+    out = torch.empty(n, device=dev)
+
+    def call():
+        _ok(lib.kz_dequantize_i8_f32(q.data_ptr(), n, 0.01, out.data_ptr(), _sh(dev)))
+    _time_launches(args, rank, dev, call, "dequantize, 2048 x 4096 codes", {"bytes": 5.0 * n})
+
+
+def _time_launches(args, rank, dev, call, name, work):
+    import torch
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    start, end = _events(dev)
+    start.record(torch.cuda.current_stream(dev))
+    for _ in range(args.steps):
+        call()
+    end.record(torch.cuda.current_stream(dev))
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) / args.steps * 1e3
+    if rank == 0:
+        line = {"metric": METRIC, "workload": name, "avg_us": us, "launches": args.steps + max(args.warmup, 1)}
+        if "op" in work:
+            line["top_s"] = work["op"] / (us / 1e6) / 1e12
+        if "bytes" in work:
+            line["gb_s"] = work["bytes"] / (us / 1e6) / 1e9
+        print(json.dumps(line))
+
+
 # ------------------------------------------------------------------- main
 
 def main():
@@ -1343,7 +1405,8 @@ def main():
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
     {"stack": run_stack, "linear": run_linear, "transformer": run_transformer, "sweep": run_sweep,
-     "mlp": run_mlp, "kernels": run_kernels, "gemm": run_gemm}[args.workload](args, rank, world, local_rank, dev)
+     "mlp": run_mlp, "kernels": run_kernels, "gemm": run_gemm, "attention": run_attention,
+     "dequantize": run_dequantize}[args.workload](args, rank, world, local_rank, dev)
 
 
 if __name__ == "__main__":

@@ -1351,9 +1351,19 @@ int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, k
     const int64_t per_block = 256 * 4 * kDeqBatch;
     float s_hi, s_lo;
     if (dequant_split_exact(scale, &s_hi, &s_lo)) {
-        // no shared memory: eight resident 256-thread blocks per SM
+        // one wave of resident blocks (the grid-stride loop spreads the tail
+        // over every thread) instead of a partial second wave
+        static std::atomic<int> resident[64];
+        int dev = 0;
+        KZ_CHECK_CUDA(cudaGetDevice(&dev));
+        int per_sm = (dev >= 0 && dev < 64) ? resident[dev] : 0;
+        if (per_sm == 0) {
+            KZ_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dequantize_split_kernel, 256, 0));
+            per_sm = std::max(per_sm, 1);
+            if (dev >= 0 && dev < 64) resident[dev] = per_sm;
+        }
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + per_block - 1) / per_block,
-                                                                     8 * (int64_t)sm_count()));
+                                                                     (int64_t)per_sm * sm_count()));
         dequantize_split_kernel<<<grid, 256, 0, s>>>(q, n, s_hi, s_lo, out);
         return launch_status("dequantize_split_kernel");
     }
