@@ -1356,7 +1356,7 @@ int kz_dequantize_i8_f32(const int8_t* q, int64_t n, double scale, float* out, k
         static std::atomic<int> resident[64];
         int dev = 0;
         KZ_CHECK_CUDA(cudaGetDevice(&dev));
-        int per_sm = (dev >= 0 && dev < 64) ? resident[dev] : 0;
+        int per_sm = (dev >= 0 && dev < 64) ? resident[dev].load() : 0;
         if (per_sm == 0) {
             KZ_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dequantize_split_kernel, 256, 0));
             per_sm = std::max(per_sm, 1);
