@@ -19,21 +19,6 @@ namespace kz {
 
 constexpr int kBM = 64, kBN = 64, kBK = 16;
 
-// Two adjacent accumulators as one packed fp32 pair: {lo, hi} += {a * b0,
-// a * b1}, each product a scalar .rn multiply, the two sums one sm_100
-// add.rn.f32x2 -- every half rounded exactly as the scalar add rounds it
-// (products stay scalar: a packed multiply whose only use is a packed add is
-// fused into a packed FMA by the code generator).
-__device__ __forceinline__ void mul_add_pair(uint64_t& acc, float a, float b0, float b1) {
-    const float p0 = __fmul_rn(a, b0), p1 = __fmul_rn(a, b1);
-    uint64_t p;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "f"(p0), "f"(p1));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc) : "l"(acc), "l"(p));
-}
-__device__ __forceinline__ void unpack_pair(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-
 __device__ __forceinline__ float act_apply(float v, int act) {
     if (act == KZ_ACT_RELU) return v > 0.0f ? v : 0.0f;
     if (act == KZ_ACT_GELU) {
@@ -147,11 +132,11 @@ __global__ void __launch_bounds__(256, 2) qlinear_w8a32_tile128_kernel(const flo
         *reinterpret_cast<float4*>(&Bs[b][wk][wc]) =
             make_float4(table[wv & 0xFFu], table[(wv >> 8) & 0xFFu], table[(wv >> 16) & 0xFFu], table[wv >> 24]);
     };
-    uint64_t acc2[8][4];                       // {acc[i][2p], acc[i][2p + 1]}
+    float acc[8][8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int p = 0; p < 4; ++p) acc2[i][p] = 0ull;   // +0.0f, +0.0f
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
     fetch(0);
     __syncthreads();   // table ready
     stage(0);
@@ -171,7 +156,7 @@ __global__ void __launch_bounds__(256, 2) qlinear_w8a32_tile128_kernel(const flo
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int p = 0; p < 4; ++p) mul_add_pair(acc2[i][p], a[i], b[2 * p], b[2 * p + 1]);
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
         }
         if (more) {
             stage(buf ^ 1);
@@ -179,11 +164,6 @@ __global__ void __launch_bounds__(256, 2) qlinear_w8a32_tile128_kernel(const flo
             buf ^= 1;
         }
     }
-    float acc[8][8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int p = 0; p < 4; ++p) unpack_pair(acc2[i][p], acc[i][2 * p], acc[i][2 * p + 1]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int64_t m = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + i - 4);
