@@ -76,6 +76,31 @@ def test_causal_mask_values_and_marker():
     assert not getattr(kz.Tensor(m.data.clone()), "causal", False)
 
 
+def test_attention_host_checks():
+    """attention_device rejects, before any device work: CPU tensors (no CPU
+    fallback), a model width that the heads do not divide, q / k / v shapes
+    that disagree, and batches that are not laid out row after row; the
+    causal flag is taken only for a causal_mask() of the exact (query, key)
+    length."""
+    import torch
+
+    from kansaiml_b200 import nn
+    from kansaiml_b200.quantize import attention_device
+    x = torch.zeros((2, 8, 64))
+    with pytest.raises(ValueError, match="CUDA"):
+        attention_device(x, x, x, 2)
+    with pytest.raises(ValueError, match="heads"):
+        attention_device(x, x, x, 3)
+    with pytest.raises(ValueError, match="do not match"):
+        attention_device(x, torch.zeros((2, 9, 64)), x, 2)
+    m = nn.causal_mask(8, device="cpu")
+    assert nn.MultiHeadAttention._causal(m, 8, 8)
+    assert not nn.MultiHeadAttention._causal(m, 8, 9)
+    assert not nn.MultiHeadAttention._causal(m, 4, 4)
+    assert not nn.MultiHeadAttention._causal(kz.Tensor(m.data.clone()), 8, 8)
+    assert not nn.MultiHeadAttention._causal(None, 8, 8)
+
+
 def test_kansai_import_path_is_this_backend():
     """The reference's import lines (tests/test_quantize.py:22-23 style) resolve
     to this backend's objects, and both packages load side by side with the
