@@ -471,7 +471,8 @@ extern "C" int kz_attention_f32(const float* q, const float* k, const float* v, 
     KZ_REQUIRE(d_k == 32 || d_k == 64 || d_k == 128, "kz_attention_f32: d_k must be 32, 64 or 128");
     KZ_REQUIRE(!causal || seq_q == seq_k, "kz_attention_f32: causal attention needs seq_q == seq_k");
     KZ_REQUIRE(batch * heads * seq_q == 0 || seq_k > 0, "kz_attention_f32: no keys");
-    KZ_REQUIRE(batch < (1 << 20) && heads < (1 << 16) && seq_q < (1 << 24) && seq_k < (1 << 24),
+    KZ_REQUIRE(batch < (1 << 20) && heads < (1 << 16) && seq_q < (1 << 24) && seq_k < (1 << 24) &&
+                   batch * heads * ((seq_q + kAttRows - 1) / kAttRows) < (int64_t)INT32_MAX,
                "kz_attention_f32: size out of range");
     if (batch * heads * seq_q == 0) {
         // no values: zero partials (an absmax of 0)
