@@ -821,10 +821,11 @@ def measure_kernels(args, rank, world, local_rank, dev):
         _ok(lib.kz_quantize_cols_f32(ws[nxt(NSETS)].data_ptr(), K_IN, N_OUT, qT.data_ptr(), s64.data_ptr(),
                                      s32.data_ptr(), wsb.data_ptr(), wsb.numel(), _sh(dev)))
     ne = K_IN * N_OUT
-    out["quantize_cols"] = _hbm_entry("absmax_cols4_kernel + quantize_cols4_kernel", _kernel_us(qcols, dev, name="quantize_cols"),
+    out["quantize_cols"] = _hbm_entry("quantize_cols_strip_kernel", _kernel_us(qcols, dev, name="quantize_cols"),
                                       9.0 * ne, hbm_gbs,
-                                      "9 B/element for the pair (absmax 4, quantize 4 + 1); the quantize pass "
-                                      "may re-read the 67 MB weight from L2", dram_bytes=5.0 * ne)
+                                      "9 B/element counted as absmax (4) + quantize (4 + 1), the accounting of a "
+                                      "two-pass form; this single pass moves 5 B/element (frac_dram)",
+                                      dram_bytes=5.0 * ne)
     del ws, qT, wsb
     # LayerNorm -> absmax partials (config 3's 8192 x 256 activations)
     Ml, Dl = 8192, 256

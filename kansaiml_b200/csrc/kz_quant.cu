@@ -877,6 +877,85 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
     }
 }
 
+// One pass over a strip of 8 whole columns (K <= 4096 rows): the strip is
+// read once into registers (each thread 16 consecutive rows x 4 columns, one
+// 16-byte load per row; a warp's loads cover 16 rows x 32 bytes, whole
+// sectors), the 8 column maxima are reduced in the block, and each thread
+// quantizes its 16 values per column from registers into one 16-byte run of
+// K-major codes (pack16: fast path + exact repair).  4 B read + 1 B written
+// per element, nothing read twice.
+constexpr int kStripCols = 8;
+constexpr int kStripThreads = 512;
+constexpr int kStripMaxK = 16 * (kStripThreads / 2);   // 4096
+
+__global__ void __launch_bounds__(kStripThreads, 1) quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K,
+                                                                           int64_t N, int8_t* __restrict__ qT,
+                                                                           double* scales, float* scales_f32,
+                                                                           int* status) {
+    __shared__ uint32_t red[kStripThreads / 32][kStripCols];
+    __shared__ ScaleInfo s_si[kStripCols];
+    const int t = threadIdx.x, half = t & 1, lane = t & 31, warp = t >> 5;
+    const int64_t n = (int64_t)blockIdx.x * kStripCols + 4 * half;
+    const int64_t k0 = 16 * (int64_t)(t >> 1);
+    const bool rows_ok = k0 < K;   // K % 16 == 0: all 16 rows or none
+    float4 v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        v[i] = rows_ok ? __ldcs(reinterpret_cast<const float4*>(w + (k0 + i) * N + n)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        m0 = max(m0, abs_bits(v[i].x));
+        m1 = max(m1, abs_bits(v[i].y));
+        m2 = max(m2, abs_bits(v[i].z));
+        m3 = max(m3, abs_bits(v[i].w));
+    }
+    // lanes of one parity hold the same four columns
+#pragma unroll
+    for (int o = 2; o < 32; o <<= 1) {
+        m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+        m3 = max(m3, __shfl_xor_sync(0xffffffffu, m3, o));
+    }
+    if (lane < 2) {
+        red[warp][4 * lane + 0] = m0;
+        red[warp][4 * lane + 1] = m1;
+        red[warp][4 * lane + 2] = m2;
+        red[warp][4 * lane + 3] = m3;
+    }
+    __syncthreads();
+    if (t < kStripCols) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
+        const ScaleInfo si = scale_from_absmax_bits(bits);
+        s_si[t] = si;
+        const int64_t c = (int64_t)blockIdx.x * kStripCols + t;
+        if (si.finite) {
+            scales[c] = si.scale;
+            if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
+        } else {
+            scales[c] = __longlong_as_double(0x7FF8000000000000ll);
+            if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
+        }
+    }
+    __syncthreads();
+    if (!rows_ok) return;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const ScaleInfo si = s_si[4 * half + j];
+        auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (si.finite)
+            out = pack16(make_float4(col(0), col(1), col(2), col(3)), make_float4(col(4), col(5), col(6), col(7)),
+                         make_float4(col(8), col(9), col(10), col(11)),
+                         make_float4(col(12), col(13), col(14), col(15)), si);
+        *reinterpret_cast<uint4*>(qT + (n + j) * K + k0) = out;
+    }
+}
+
 // --------------------------------------------------------- per-row (tokens)
 
 // One block per row: absmax then quantize of that row.
@@ -1243,8 +1322,16 @@ static int64_t col_splits(int64_t K, int64_t N, bool vec) {
 // Both per-channel quantize entry points: `partial` holds at least
 // max_words words of scratch (splits x N are used).
 static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT, double* scales, float* scales_f32,
-                                uint32_t* partial, int64_t max_words, cudaStream_t s, const char* who) {
+                                uint32_t* partial, int64_t max_words, cudaStream_t s, const char* who,
+                                bool allow_strip = false) {
     const bool vec = cols_vectorised(w, K, N, qT);
+    if (allow_strip && vec && K <= kStripMaxK && N % kStripCols == 0) {
+        // whole columns fit one block's registers: a single pass, no workspace
+        KZ_REQUIRE(N / kStripCols < INT32_MAX, "quantize_cols: N too large");
+        quantize_cols_strip_kernel<<<(unsigned)(N / kStripCols), kStripThreads, 0, s>>>(w, K, N, qT, scales,
+                                                                                     scales_f32, device_status_ptr());
+        return launch_status(who);
+    }
     int64_t splits = K == 0 ? 1 : col_splits(K, N, vec);
     if (splits * N > max_words) splits = std::max<int64_t>(1, max_words / N);
     KZ_REQUIRE(splits * N <= max_words, "quantize_cols: scratch smaller than N words");
@@ -1297,7 +1384,7 @@ int kz_quantize_cols_f32(const float* w, int64_t K, int64_t N, int8_t* qT, doubl
                "kz_quantize_cols_f32: workspace smaller than kz_quantize_cols_workspace_bytes(K, N)");
     return quantize_cols_launch(w, K, N, qT, scales, scales_f32, static_cast<uint32_t*>(workspace),
                                 (int64_t)(workspace_bytes / sizeof(uint32_t)), reinterpret_cast<cudaStream_t>(stream),
-                                "kz_quantize_cols_f32");
+                                "kz_quantize_cols_f32", /*allow_strip=*/true);
 }
 
 int kz_quantize_rows_f32(const float* x, int64_t M, int64_t K, int8_t* q, double* scales, float* scales_f32,
