@@ -877,26 +877,38 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
     }
 }
 
-// One pass over a strip of 8 whole columns (K <= 4096 rows): the strip is
-// read once into registers (each thread 16 consecutive rows x 4 columns, one
-// 16-byte load per row; a warp's loads cover 16 rows x 32 bytes, whole
-// sectors), the 8 column maxima are reduced in the block, and each thread
+// One pass over a strip of 8 whole columns (K <= 4096 rows).  A cluster of
+// two 256-thread blocks shares the strip: block r of the pair reads rows
+// [2048 r, 2048 r + 2048) once into registers (each thread 16 consecutive
+// rows x 4 columns, one 16-byte load per row; a warp's loads cover 16 rows x
+// 32 bytes, whole sectors), reduces its 8 column maxima, and the pair
+// exchanges them through distributed shared memory; each thread then
 // quantizes its 16 values per column from registers into one 16-byte run of
 // K-major codes (pack16: fast path + exact repair).  4 B read + 1 B written
-// per element, nothing read twice.
+// per element, nothing read twice; two blocks per SM, so one block's loads
+// overlap another's arithmetic.
 constexpr int kStripCols = 8;
-constexpr int kStripThreads = 512;
-constexpr int kStripMaxK = 16 * (kStripThreads / 2);   // 4096
+constexpr int kStripThreads = 256;
+constexpr int kStripRowsPerBlock = 16 * (kStripThreads / 2);   // 2048
+constexpr int kStripMaxK = 2 * kStripRowsPerBlock;              // 4096
 
-__global__ void __launch_bounds__(kStripThreads, 1) quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K,
-                                                                           int64_t N, int8_t* __restrict__ qT,
-                                                                           double* scales, float* scales_f32,
-                                                                           int* status) {
+__device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kStripThreads, 2)
+    quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K, int64_t N, int8_t* __restrict__ qT,
+                               double* scales, float* scales_f32, int* status) {
     __shared__ uint32_t red[kStripThreads / 32][kStripCols];
+    __shared__ uint32_t block_max[kStripCols];   // this block's column maxima, read by the other block
     __shared__ ScaleInfo s_si[kStripCols];
+    const uint32_t rank = cluster_ctarank();    // which half of the rows
     const int t = threadIdx.x, half = t & 1, lane = t & 31, warp = t >> 5;
-    const int64_t n = (int64_t)blockIdx.x * kStripCols + 4 * half;
-    const int64_t k0 = 16 * (int64_t)(t >> 1);
+    const int64_t c0 = (int64_t)(blockIdx.x >> 1) * kStripCols;
+    const int64_t n = c0 + 4 * half;
+    const int64_t k0 = (int64_t)rank * kStripRowsPerBlock + 16 * (int64_t)(t >> 1);
     const bool rows_ok = k0 < K;   // K % 16 == 0: all 16 rows or none
     float4 v[16];
 #pragma unroll
@@ -929,16 +941,25 @@ __global__ void __launch_bounds__(kStripThreads, 1) quantize_cols_strip_kernel(c
         uint32_t bits = 0;
 #pragma unroll
         for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
-        const ScaleInfo si = scale_from_absmax_bits(bits);
+        block_max[t] = bits;
+    }
+    cluster_sync();   // both blocks' maxima written
+    uint32_t other = 0;
+    if (t < kStripCols) other = ld_shared_cluster_u32(mapa_shared(smem_u32(&block_max[t]), rank ^ 1u));
+    cluster_sync();   // both blocks done reading the other's maxima (it may now exit)
+    if (t < kStripCols) {
+        const ScaleInfo si = scale_from_absmax_bits(max(block_max[t], other));
         s_si[t] = si;
-        const int64_t c = (int64_t)blockIdx.x * kStripCols + t;
-        if (si.finite) {
-            scales[c] = si.scale;
-            if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
-        } else {
-            scales[c] = __longlong_as_double(0x7FF8000000000000ll);
-            if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
-            record_status(status, KZ_ERR_NONFINITE);
+        const int64_t c = c0 + t;
+        if (rank == 0) {
+            if (si.finite) {
+                scales[c] = si.scale;
+                if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
+            } else {
+                scales[c] = __longlong_as_double(0x7FF8000000000000ll);
+                if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
+                record_status(status, KZ_ERR_NONFINITE);
+            }
         }
     }
     __syncthreads();
@@ -1327,9 +1348,9 @@ static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT
     const bool vec = cols_vectorised(w, K, N, qT);
     if (allow_strip && vec && K <= kStripMaxK && N % kStripCols == 0) {
         // whole columns fit one block's registers: a single pass, no workspace
-        KZ_REQUIRE(N / kStripCols < INT32_MAX, "quantize_cols: N too large");
-        quantize_cols_strip_kernel<<<(unsigned)(N / kStripCols), kStripThreads, 0, s>>>(w, K, N, qT, scales,
-                                                                                     scales_f32, device_status_ptr());
+        KZ_REQUIRE(N / kStripCols < INT32_MAX / 2, "quantize_cols: N too large");
+        quantize_cols_strip_kernel<<<(unsigned)(2 * (N / kStripCols)), kStripThreads, 0, s>>>(
+            w, K, N, qT, scales, scales_f32, device_status_ptr());
         return launch_status(who);
     }
     int64_t splits = K == 0 ? 1 : col_splits(K, N, vec);
