@@ -877,20 +877,20 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
     }
 }
 
-// One pass over a strip of 8 whole columns (K <= 4096 rows).  A cluster of
-// two 256-thread blocks shares the strip: block r of the pair reads rows
-// [2048 r, 2048 r + 2048) once into registers (each thread 16 consecutive
-// rows x 4 columns, one 16-byte load per row; a warp's loads cover 16 rows x
-// 32 bytes, whole sectors), reduces its 8 column maxima, and the pair
-// exchanges them through distributed shared memory; each thread then
-// quantizes its 16 values per column from registers into one 16-byte run of
-// K-major codes (pack16: fast path + exact repair).  4 B read + 1 B written
-// per element, nothing read twice; two blocks per SM, so one block's loads
-// overlap another's arithmetic.
-constexpr int kStripCols = 8;
+// One pass over a strip of 32 whole columns (K <= 4096 rows).  A cluster of
+// eight 256-thread blocks shares the strip: block r reads rows [512 r,
+// 512 r + 512) once into registers (each thread 16 consecutive rows x 4
+// columns, one 16-byte load per row; a warp's loads cover 4 rows x 128
+// bytes, whole lines), reduces its 32 column maxima, and the blocks exchange
+// them through distributed shared memory; each thread then quantizes its 16
+// values per column from registers into one 16-byte run of K-major codes
+// (pack16: fast path + exact repair).  4 B read + 1 B written per element,
+// nothing read twice.
+constexpr int kStripCols = 32;
 constexpr int kStripThreads = 256;
-constexpr int kStripRowsPerBlock = 16 * (kStripThreads / 2);   // 2048
-constexpr int kStripMaxK = 2 * kStripRowsPerBlock;              // 4096
+constexpr int kStripBlocks = 8;                                           // cluster size
+constexpr int kStripRowsPerBlock = 16 * (kStripThreads / (kStripCols / 4));   // 512
+constexpr int kStripMaxK = kStripBlocks * kStripRowsPerBlock;               // 4096
 
 __device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr) {
     uint32_t v;
@@ -898,17 +898,17 @@ __device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr)
     return v;
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kStripThreads, 2)
+__global__ void __cluster_dims__(kStripBlocks, 1, 1) __launch_bounds__(kStripThreads, 2)
     quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K, int64_t N, int8_t* __restrict__ qT,
                                double* scales, float* scales_f32, int* status) {
     __shared__ uint32_t red[kStripThreads / 32][kStripCols];
-    __shared__ uint32_t block_max[kStripCols];   // this block's column maxima, read by the other block
+    __shared__ uint32_t block_max[kStripCols];   // this block's column maxima, read by the others
     __shared__ ScaleInfo s_si[kStripCols];
-    const uint32_t rank = cluster_ctarank();    // which half of the rows
-    const int t = threadIdx.x, half = t & 1, lane = t & 31, warp = t >> 5;
-    const int64_t c0 = (int64_t)(blockIdx.x >> 1) * kStripCols;
-    const int64_t n = c0 + 4 * half;
-    const int64_t k0 = (int64_t)rank * kStripRowsPerBlock + 16 * (int64_t)(t >> 1);
+    const uint32_t rank = cluster_ctarank();    // which 512 rows
+    const int t = threadIdx.x, cg = t & 7, lane = t & 31, warp = t >> 5;
+    const int64_t c0 = (int64_t)(blockIdx.x / kStripBlocks) * kStripCols;
+    const int64_t n = c0 + 4 * cg;
+    const int64_t k0 = (int64_t)rank * kStripRowsPerBlock + 16 * (int64_t)(t >> 3);
     const bool rows_ok = k0 < K;   // K % 16 == 0: all 16 rows or none
     float4 v[16];
 #pragma unroll
@@ -922,15 +922,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kStripThreads, 2)
         m2 = max(m2, abs_bits(v[i].z));
         m3 = max(m3, abs_bits(v[i].w));
     }
-    // lanes of one parity hold the same four columns
+    // lanes with the same lane % 8 hold the same four columns
 #pragma unroll
-    for (int o = 2; o < 32; o <<= 1) {
+    for (int o = 8; o < 32; o <<= 1) {
         m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
         m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
         m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
         m3 = max(m3, __shfl_xor_sync(0xffffffffu, m3, o));
     }
-    if (lane < 2) {
+    if (lane < 8) {
         red[warp][4 * lane + 0] = m0;
         red[warp][4 * lane + 1] = m1;
         red[warp][4 * lane + 2] = m2;
@@ -943,12 +943,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kStripThreads, 2)
         for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
         block_max[t] = bits;
     }
-    cluster_sync();   // both blocks' maxima written
-    uint32_t other = 0;
-    if (t < kStripCols) other = ld_shared_cluster_u32(mapa_shared(smem_u32(&block_max[t]), rank ^ 1u));
-    cluster_sync();   // both blocks done reading the other's maxima (it may now exit)
+    cluster_sync();   // every block's maxima written
+    uint32_t all = 0;
     if (t < kStripCols) {
-        const ScaleInfo si = scale_from_absmax_bits(max(block_max[t], other));
+        const uint32_t addr = smem_u32(&block_max[t]);
+#pragma unroll
+        for (int r = 0; r < kStripBlocks; ++r) all = max(all, ld_shared_cluster_u32(mapa_shared(addr, (uint32_t)r)));
+    }
+    cluster_sync();   // every block done reading the others' maxima (they may now exit)
+    if (t < kStripCols) {
+        const ScaleInfo si = scale_from_absmax_bits(all);
         s_si[t] = si;
         const int64_t c = c0 + t;
         if (rank == 0) {
@@ -966,7 +970,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kStripThreads, 2)
     if (!rows_ok) return;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const ScaleInfo si = s_si[4 * half + j];
+        const ScaleInfo si = s_si[4 * cg + j];
         auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
         uint4 out = make_uint4(0u, 0u, 0u, 0u);
         if (si.finite)
@@ -1348,8 +1352,8 @@ static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT
     const bool vec = cols_vectorised(w, K, N, qT);
     if (allow_strip && vec && K <= kStripMaxK && N % kStripCols == 0) {
         // whole columns fit one block's registers: a single pass, no workspace
-        KZ_REQUIRE(N / kStripCols < INT32_MAX / 2, "quantize_cols: N too large");
-        quantize_cols_strip_kernel<<<(unsigned)(2 * (N / kStripCols)), kStripThreads, 0, s>>>(
+        KZ_REQUIRE(N / kStripCols < INT32_MAX / kStripBlocks, "quantize_cols: N too large");
+        quantize_cols_strip_kernel<<<(unsigned)(kStripBlocks * (N / kStripCols)), kStripThreads, 0, s>>>(
             w, K, N, qT, scales, scales_f32, device_status_ptr());
         return launch_status(who);
     }
