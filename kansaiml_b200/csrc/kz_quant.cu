@@ -877,38 +877,26 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
     }
 }
 
-// One pass over a strip of 32 whole columns (K <= 4096 rows).  A cluster of
-// eight 256-thread blocks shares the strip: block r reads rows [512 r,
-// 512 r + 512) once into registers (each thread 16 consecutive rows x 4
-// columns, one 16-byte load per row; a warp's loads cover 4 rows x 128
-// bytes, whole lines), reduces its 32 column maxima, and the blocks exchange
-// them through distributed shared memory; each thread then quantizes its 16
-// values per column from registers into one 16-byte run of K-major codes
-// (pack16: fast path + exact repair).  4 B read + 1 B written per element,
-// nothing read twice.
-constexpr int kStripCols = 32;
-constexpr int kStripThreads = 256;
-constexpr int kStripBlocks = 8;                                           // cluster size
-constexpr int kStripRowsPerBlock = 16 * (kStripThreads / (kStripCols / 4));   // 512
-constexpr int kStripMaxK = kStripBlocks * kStripRowsPerBlock;               // 4096
+// One pass over a strip of 8 whole columns (K <= 4096 rows): the strip is
+// read once into registers (each thread 16 consecutive rows x 4 columns, one
+// 16-byte load per row; a warp's loads cover 16 rows x 32 bytes, whole
+// sectors), the 8 column maxima are reduced in the block, and each thread
+// quantizes its 16 values per column from registers into one 16-byte run of
+// K-major codes (pack16: fast path + exact repair).  4 B read + 1 B written
+// per element, nothing read twice.
+constexpr int kStripCols = 8;
+constexpr int kStripThreads = 512;
+constexpr int kStripMaxK = 16 * (kStripThreads / 2);   // 4096
 
-__device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr) {
-    uint32_t v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
-    return v;
-}
-
-__global__ void __cluster_dims__(kStripBlocks, 1, 1) __launch_bounds__(kStripThreads, 2)
-    quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K, int64_t N, int8_t* __restrict__ qT,
-                               double* scales, float* scales_f32, int* status) {
+__global__ void __launch_bounds__(kStripThreads, 1) quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K,
+                                                                           int64_t N, int8_t* __restrict__ qT,
+                                                                           double* scales, float* scales_f32,
+                                                                           int* status) {
     __shared__ uint32_t red[kStripThreads / 32][kStripCols];
-    __shared__ uint32_t block_max[kStripCols];   // this block's column maxima, read by the others
     __shared__ ScaleInfo s_si[kStripCols];
-    const uint32_t rank = cluster_ctarank();    // which 512 rows
-    const int t = threadIdx.x, cg = t & 7, lane = t & 31, warp = t >> 5;
-    const int64_t c0 = (int64_t)(blockIdx.x / kStripBlocks) * kStripCols;
-    const int64_t n = c0 + 4 * cg;
-    const int64_t k0 = (int64_t)rank * kStripRowsPerBlock + 16 * (int64_t)(t >> 3);
+    const int t = threadIdx.x, half = t & 1, lane = t & 31, warp = t >> 5;
+    const int64_t n = (int64_t)blockIdx.x * kStripCols + 4 * half;
+    const int64_t k0 = 16 * (int64_t)(t >> 1);
     const bool rows_ok = k0 < K;   // K % 16 == 0: all 16 rows or none
     float4 v[16];
 #pragma unroll
@@ -922,15 +910,15 @@ __global__ void __cluster_dims__(kStripBlocks, 1, 1) __launch_bounds__(kStripThr
         m2 = max(m2, abs_bits(v[i].z));
         m3 = max(m3, abs_bits(v[i].w));
     }
-    // lanes with the same lane % 8 hold the same four columns
+    // lanes of one parity hold the same four columns
 #pragma unroll
-    for (int o = 8; o < 32; o <<= 1) {
+    for (int o = 2; o < 32; o <<= 1) {
         m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
         m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
         m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
         m3 = max(m3, __shfl_xor_sync(0xffffffffu, m3, o));
     }
-    if (lane < 8) {
+    if (lane < 2) {
         red[warp][4 * lane + 0] = m0;
         red[warp][4 * lane + 1] = m1;
         red[warp][4 * lane + 2] = m2;
@@ -941,36 +929,23 @@ __global__ void __cluster_dims__(kStripBlocks, 1, 1) __launch_bounds__(kStripThr
         uint32_t bits = 0;
 #pragma unroll
         for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
-        block_max[t] = bits;
-    }
-    cluster_sync();   // every block's maxima written
-    uint32_t all = 0;
-    if (t < kStripCols) {
-        const uint32_t addr = smem_u32(&block_max[t]);
-#pragma unroll
-        for (int r = 0; r < kStripBlocks; ++r) all = max(all, ld_shared_cluster_u32(mapa_shared(addr, (uint32_t)r)));
-    }
-    cluster_sync();   // every block done reading the others' maxima (they may now exit)
-    if (t < kStripCols) {
-        const ScaleInfo si = scale_from_absmax_bits(all);
+        const ScaleInfo si = scale_from_absmax_bits(bits);
         s_si[t] = si;
-        const int64_t c = c0 + t;
-        if (rank == 0) {
-            if (si.finite) {
-                scales[c] = si.scale;
-                if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
-            } else {
-                scales[c] = __longlong_as_double(0x7FF8000000000000ll);
-                if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
-                record_status(status, KZ_ERR_NONFINITE);
-            }
+        const int64_t c = (int64_t)blockIdx.x * kStripCols + t;
+        if (si.finite) {
+            scales[c] = si.scale;
+            if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
+        } else {
+            scales[c] = __longlong_as_double(0x7FF8000000000000ll);
+            if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
         }
     }
     __syncthreads();
     if (!rows_ok) return;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const ScaleInfo si = s_si[4 * cg + j];
+        const ScaleInfo si = s_si[4 * half + j];
         auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
         uint4 out = make_uint4(0u, 0u, 0u, 0u);
         if (si.finite)
@@ -1350,11 +1325,12 @@ static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT
                                 uint32_t* partial, int64_t max_words, cudaStream_t s, const char* who,
                                 bool allow_strip = false) {
     const bool vec = cols_vectorised(w, K, N, qT);
-    if (allow_strip && vec && K <= kStripMaxK && N % kStripCols == 0) {
-        // whole columns fit one block's registers: a single pass, no workspace
-        KZ_REQUIRE(N / kStripCols < INT32_MAX / kStripBlocks, "quantize_cols: N too large");
-        quantize_cols_strip_kernel<<<(unsigned)(kStripBlocks * (N / kStripCols)), kStripThreads, 0, s>>>(
-            w, K, N, qT, scales, scales_f32, device_status_ptr());
+    if (allow_strip && vec && K > kStripMaxK / 2 && K <= kStripMaxK && N % kStripCols == 0) {
+        // whole columns fit one block's registers (and fill most of its
+        // threads): a single pass, no workspace
+        KZ_REQUIRE(N / kStripCols < INT32_MAX, "quantize_cols: N too large");
+        quantize_cols_strip_kernel<<<(unsigned)(N / kStripCols), kStripThreads, 0, s>>>(w, K, N, qT, scales,
+                                                                                     scales_f32, device_status_ptr());
         return launch_status(who);
     }
     int64_t splits = K == 0 ? 1 : col_splits(K, N, vec);
