@@ -80,11 +80,12 @@ def parse():
                          "(ce), copy-engine pulls feeding the gated GEMM (peer) or the all-gather inside the GEMM "
                          "launch (fused)")
     ap.add_argument("--workload", choices=["stack", "linear", "transformer", "sweep", "mlp", "kernels", "gemm",
-                                           "attention", "dequantize"],
+                                           "attention", "dequantize", "quantize_cols"],
                     default="stack",
                     help="stack: config 5 (default); linear: config 2; transformer: config 3; sweep: config 4; "
                          "mlp: config 1; kernels: the per-kernel entries alone; gemm: one GEMM shape (--shape); "
-                         "attention / dequantize: that kernel alone at its bench shape (profiling targets)")
+                         "attention / dequantize / quantize_cols: that kernel alone at its bench shape "
+                         "(profiling targets)")
     ap.add_argument("--shape", default="8192,16384,16384", help="gemm workload: M,N,K")
     ap.add_argument("--tp", type=int, default=None,
                     help="stack: column-sharding group size (default: the stack's, N up to 4, else 4)")
@@ -1352,6 +1353,27 @@ def run_dequantize(args, rank, world, local_rank, dev):
     _time_launches(args, rank, dev, call, "dequantize, 2048 x 4096 codes", {"bytes": 5.0 * n})
 
 
+def run_quantize_cols(args, rank, world, local_rank, dev):
+    """kz_quantize_cols_f32 on config 2's 4096 x 4096 weight (per-channel
+    int8, K-major codes): W + K launches, CUDA events around the K; a
+    profiling target."""
+    import torch
+    from kansaiml_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device=dev)
+    g.manual_seed(K_IN)
+    w = torch.randn((K_IN, N_OUT), generator=g, device=dev) * 0.02
+    qT = torch.empty((N_OUT, K_IN), dtype=torch.int8, device=dev)
+    s64 = torch.empty(N_OUT, dtype=torch.float64, device=dev)
+    s32 = torch.empty(N_OUT, device=dev)
+    ws = torch.empty(lib.kz_quantize_cols_workspace_bytes(K_IN, N_OUT), dtype=torch.uint8, device=dev)
+
+    def call():
+        _ok(lib.kz_quantize_cols_f32(w.data_ptr(), K_IN, N_OUT, qT.data_ptr(), s64.data_ptr(), s32.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), _sh(dev)))
+    _time_launches(args, rank, dev, call, "per-channel weight quantize, 4096 x 4096", {"bytes": 5.0 * K_IN * N_OUT})
+
+
 def _time_launches(args, rank, dev, call, name, work):
     import torch
     for _ in range(max(args.warmup, 1)):
@@ -1407,7 +1429,8 @@ def main():
             os.close(saved_fd)
     {"stack": run_stack, "linear": run_linear, "transformer": run_transformer, "sweep": run_sweep,
      "mlp": run_mlp, "kernels": run_kernels, "gemm": run_gemm, "attention": run_attention,
-     "dequantize": run_dequantize}[args.workload](args, rank, world, local_rank, dev)
+     "dequantize": run_dequantize, "quantize_cols": run_quantize_cols}[args.workload](args, rank, world, local_rank,
+                                                                                     dev)
 
 
 if __name__ == "__main__":
