@@ -877,121 +877,83 @@ __global__ void __launch_bounds__(256) quantize_cols4_kernel(const float* __rest
     }
 }
 
-// One pass over strips of 8 whole columns (K <= 4096 rows), persistent: one
-// 512-thread block per SM walks strips blockIdx.x, + gridDim.x, ...  While it
-// quantizes strip s from registers, strip s + gridDim.x streams into shared
-// memory by cp.async (16-byte copies, no registers), so the SM's loads and
-// its arithmetic overlap instead of alternating.  Per strip each thread owns
-// 16 consecutive rows x 4 columns (a warp's copies cover 16 rows x 32 bytes,
-// whole sectors); the 8 column maxima are reduced in the block and each
-// thread turns its 16 values per column into one 16-byte run of K-major
-// codes (pack16: fast path + exact repair).  4 B read + 1 B written per
-// element, nothing read twice.  Shared layout: row r at float r * 8 +
-// (r / 16) * 8, so the 16-byte reads of a quarter-warp (4 row blocks x 2
-// halves) fall in 8 distinct bank groups.
+// One pass over a strip of 8 whole columns (K <= 4096 rows): the strip is
+// read once into registers (each thread 16 consecutive rows x 4 columns, one
+// 16-byte load per row; a warp's loads cover 16 rows x 32 bytes, whole
+// sectors), the 8 column maxima are reduced in the block, and each thread
+// quantizes its 16 values per column from registers into one 16-byte run of
+// K-major codes (pack16: fast path + exact repair).  4 B read + 1 B written
+// per element, nothing read twice.
 constexpr int kStripCols = 8;
 constexpr int kStripThreads = 512;
 constexpr int kStripMaxK = 16 * (kStripThreads / 2);   // 4096
-constexpr int kStripSmemFloats = kStripMaxK * kStripCols + (kStripMaxK / 16) * 8;
-constexpr size_t kStripSmemBytes = (size_t)kStripSmemFloats * sizeof(float);   // 136 KB
-
-__device__ __forceinline__ int strip_offset(int r) { return r * kStripCols + (r >> 4) * 8; }
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kStripThreads, 1) quantize_cols_strip_kernel(const float* __restrict__ w, int64_t K,
                                                                            int64_t N, int8_t* __restrict__ qT,
                                                                            double* scales, float* scales_f32,
                                                                            int* status) {
-    extern __shared__ __align__(16) float strip[];
     __shared__ uint32_t red[kStripThreads / 32][kStripCols];
     __shared__ ScaleInfo s_si[kStripCols];
     const int t = threadIdx.x, half = t & 1, lane = t & 31, warp = t >> 5;
-    const int r0 = 16 * (t >> 1);
-    const bool rows_ok = r0 < K;   // K % 16 == 0: all 16 rows or none
-    const int64_t nstrips = N / kStripCols;
-    auto issue = [&](int64_t sidx) {
-        if (!rows_ok) return;
-        const float* src = w + (int64_t)r0 * N + sidx * kStripCols + 4 * half;
+    const int64_t n = (int64_t)blockIdx.x * kStripCols + 4 * half;
+    const int64_t k0 = 16 * (int64_t)(t >> 1);
+    const bool rows_ok = k0 < K;   // K % 16 == 0: all 16 rows or none
+    float4 v[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            cp_async16(smem_u32(strip + strip_offset(r0 + i) + 4 * half), src + (int64_t)i * N);
-    };
-    if (blockIdx.x < nstrips) issue(blockIdx.x);
-    cp_async_commit();
-    for (int64_t sidx = blockIdx.x; sidx < nstrips; sidx += gridDim.x) {
-        cp_async_wait_all();
-        __syncthreads();   // strip sidx is in shared memory; red / s_si of the previous strip are no longer read
-        float4 v[16];
+    for (int i = 0; i < 16; ++i)
+        v[i] = rows_ok ? __ldcs(reinterpret_cast<const float4*>(w + (k0 + i) * N + n)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            v[i] = rows_ok ? *reinterpret_cast<const float4*>(strip + strip_offset(r0 + i) + 4 * half)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-        __syncthreads();   // every thread has its values: the buffer takes the next strip
-        if (sidx + gridDim.x < nstrips) issue(sidx + gridDim.x);
-        cp_async_commit();
-        uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+    for (int i = 0; i < 16; ++i) {
+        m0 = max(m0, abs_bits(v[i].x));
+        m1 = max(m1, abs_bits(v[i].y));
+        m2 = max(m2, abs_bits(v[i].z));
+        m3 = max(m3, abs_bits(v[i].w));
+    }
+    // lanes of one parity hold the same four columns
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            m0 = max(m0, abs_bits(v[i].x));
-            m1 = max(m1, abs_bits(v[i].y));
-            m2 = max(m2, abs_bits(v[i].z));
-            m3 = max(m3, abs_bits(v[i].w));
-        }
-        // lanes of one parity hold the same four columns
+    for (int o = 2; o < 32; o <<= 1) {
+        m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+        m3 = max(m3, __shfl_xor_sync(0xffffffffu, m3, o));
+    }
+    if (lane < 2) {
+        red[warp][4 * lane + 0] = m0;
+        red[warp][4 * lane + 1] = m1;
+        red[warp][4 * lane + 2] = m2;
+        red[warp][4 * lane + 3] = m3;
+    }
+    __syncthreads();
+    if (t < kStripCols) {
+        uint32_t bits = 0;
 #pragma unroll
-        for (int o = 2; o < 32; o <<= 1) {
-            m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-            m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
-            m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
-            m3 = max(m3, __shfl_xor_sync(0xffffffffu, m3, o));
-        }
-        if (lane < 2) {
-            red[warp][4 * lane + 0] = m0;
-            red[warp][4 * lane + 1] = m1;
-            red[warp][4 * lane + 2] = m2;
-            red[warp][4 * lane + 3] = m3;
-        }
-        __syncthreads();
-        const int64_t c0 = sidx * kStripCols;
-        if (t < kStripCols) {
-            uint32_t bits = 0;
-#pragma unroll
-            for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
-            const ScaleInfo si = scale_from_absmax_bits(bits);
-            s_si[t] = si;
-            const int64_t c = c0 + t;
-            if (si.finite) {
-                scales[c] = si.scale;
-                if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
-            } else {
-                scales[c] = __longlong_as_double(0x7FF8000000000000ll);
-                if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
-                record_status(status, KZ_ERR_NONFINITE);
-            }
-        }
-        __syncthreads();
-        if (rows_ok) {
-            const int64_t n = c0 + 4 * half;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const ScaleInfo si = s_si[4 * half + j];
-                auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
-                uint4 out = make_uint4(0u, 0u, 0u, 0u);
-                if (si.finite)
-                    out = pack16(make_float4(col(0), col(1), col(2), col(3)),
-                                 make_float4(col(4), col(5), col(6), col(7)),
-                                 make_float4(col(8), col(9), col(10), col(11)),
-                                 make_float4(col(12), col(13), col(14), col(15)), si);
-                *reinterpret_cast<uint4*>(qT + (n + j) * K + r0) = out;
-            }
+        for (int r = 0; r < kStripThreads / 32; ++r) bits = max(bits, red[r][t]);
+        const ScaleInfo si = scale_from_absmax_bits(bits);
+        s_si[t] = si;
+        const int64_t c = (int64_t)blockIdx.x * kStripCols + t;
+        if (si.finite) {
+            scales[c] = si.scale;
+            if (scales_f32) scales_f32[c] = __double2float_rn(si.scale);
+        } else {
+            scales[c] = __longlong_as_double(0x7FF8000000000000ll);
+            if (scales_f32) scales_f32[c] = __uint_as_float(0x7FC00000u);
+            record_status(status, KZ_ERR_NONFINITE);
         }
     }
-    cp_async_wait_all();   // nothing may be in flight when the block exits
+    __syncthreads();
+    if (!rows_ok) return;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const ScaleInfo si = s_si[4 * half + j];
+        auto col = [&](int i) { return j == 0 ? v[i].x : j == 1 ? v[i].y : j == 2 ? v[i].z : v[i].w; };
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (si.finite)
+            out = pack16(make_float4(col(0), col(1), col(2), col(3)), make_float4(col(4), col(5), col(6), col(7)),
+                         make_float4(col(8), col(9), col(10), col(11)),
+                         make_float4(col(12), col(13), col(14), col(15)), si);
+        *reinterpret_cast<uint4*>(qT + (n + j) * K + k0) = out;
+    }
 }
 
 // --------------------------------------------------------- per-row (tokens)
@@ -1366,17 +1328,9 @@ static int quantize_cols_launch(const float* w, int64_t K, int64_t N, int8_t* qT
     if (allow_strip && vec && K > kStripMaxK / 2 && K <= kStripMaxK && N % kStripCols == 0) {
         // whole columns fit one block's registers (and fill most of its
         // threads): a single pass, no workspace
-        static std::atomic<int> attr_set[64];
-        int dev = 0;
-        KZ_CHECK_CUDA(cudaGetDevice(&dev));
-        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-            KZ_CHECK_CUDA(cudaFuncSetAttribute(quantize_cols_strip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)kStripSmemBytes));
-            if (dev >= 0 && dev < 64) attr_set[dev] = 1;
-        }
-        const int grid = (int)std::min<int64_t>(N / kStripCols, sm_count());
-        quantize_cols_strip_kernel<<<grid, kStripThreads, kStripSmemBytes, s>>>(w, K, N, qT, scales, scales_f32,
-                                                                               device_status_ptr());
+        KZ_REQUIRE(N / kStripCols < INT32_MAX, "quantize_cols: N too large");
+        quantize_cols_strip_kernel<<<(unsigned)(N / kStripCols), kStripThreads, 0, s>>>(w, K, N, qT, scales,
+                                                                                     scales_f32, device_status_ptr());
         return launch_status(who);
     }
     int64_t splits = K == 0 ? 1 : col_splits(K, N, vec);
