@@ -84,9 +84,10 @@ def test_qlinear_w8a32_bit_exact_vs_reference():
         for act, key in ((0, "y"), (1, "y_relu")):
             y = ocpu.qlinear_w8a32(x, q, s, b, act=act)
             assert y.tobytes() == g[f"c{i}__{key}"].tobytes(), (i, key)
-        # gelu goes through erff, identical libm here
+        # gelu: the same glibc erff and operation order as the reference's
+        # gelu_fwd (Ops.cpp:250-256), so bit for bit as well
         y = ocpu.qlinear_w8a32(x, q, s, b, act=2)
-        np.testing.assert_allclose(y, g[f"c{i}__y_gelu"], rtol=0, atol=1e-6)
+        assert y.tobytes() == g[f"c{i}__y_gelu"].tobytes(), (i, "gelu")
 
 
 def test_mlp_config1_vs_reference():
@@ -345,3 +346,34 @@ def test_attention_oracle_vs_reference_random_shapes():
         y = mha.forward(from_np(q), from_np(k), from_np(v), mask=from_np(mask) if mask is not None else None)
         ref = np.asarray(y.tolist(), np.float32).reshape(B, Sq, D)
         assert ocpu.attention(q, k, v, H, mask=mask, exp="libm").tobytes() == ref.tobytes(), (case, B, H, dk, Sq, Sk)
+
+
+@pytest.mark.skipif(not refpkg.reference_available(), reason="reference checkout / compiled core not present")
+def test_layernorm_oracle_vs_reference_random_shapes():
+    """Beyond the fixtures: the reference's own nn.LayerNorm at random row
+    counts and widths (1-300), with random gamma / beta and the residual sum,
+    against the oracle -- bit for bit."""
+    kansai = refpkg.import_reference_kansai()
+    from kansai_reference import nn
+    core = kansai.core
+
+    def from_np(x):
+        return core.from_flat(np.asarray(x, np.float32).ravel().tolist(), list(x.shape))
+
+    def to_np(t):
+        return np.asarray(t.tolist(), np.float32).reshape(list(t.shape))
+
+    rs = np.random.RandomState(91)
+    for case in range(10):
+        M, D = int(rs.randint(1, 40)), int(rs.randint(1, 301))
+        x = (rs.standard_normal((M, D)) * rs.uniform(0.1, 10) + rs.uniform(-3, 3)).astype(np.float32)
+        res = rs.standard_normal((M, D)).astype(np.float32)
+        gamma = rs.uniform(0.5, 1.5, D).astype(np.float32)
+        beta = (rs.standard_normal(D) * 0.1).astype(np.float32)
+        ln = nn.LayerNorm(D)
+        ln.weight, ln.bias = from_np(gamma), from_np(beta)
+        total = from_np(x).add(from_np(res))
+        ref = to_np(ln(total))
+        y, tot = ocpu.layernorm(x, gamma, beta, 1e-5, residual=res)
+        assert tot.tobytes() == to_np(total).tobytes(), case
+        assert y.tobytes() == ref.tobytes(), (case, M, D)
