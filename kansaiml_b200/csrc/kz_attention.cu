@@ -11,35 +11,39 @@
 //                                 the reciprocal 1/x (Tensor.cpp:677-679, Ops.cpp:213-215)
 //   attended = weights.matmul(v)  key index ascending
 // This kernel computes the same values with the same roundings: every
-// product and every sum is a separately rounded fp32 operation (__fmul_rn /
-// __fadd_rn, never contracted into an FMA) taken in the reference's index
-// order.  The one operation it cannot take from the reference is exp: the
-// reference calls the host libm's expf; here exp is rounded correctly from a
-// double-precision exp (CUDA's exp(double), error below 1 ulp of double), which
-// equals the host's expf wherever that one is correctly rounded.
+// product and every sum is a separately rounded fp32 operation (scalar .rn
+// multiplies, packed .rn adds; the file is built with --fmad=false and no
+// multiply feeds an add it could be fused with) taken in the reference's
+// index order.  The one operation it cannot take from the reference is exp:
+// the reference calls the host libm's expf; here exp is rounded correctly
+// from a double-precision exp (CUDA's exp(double), error below 1 ulp of
+// double), which equals the host's expf wherever that one is correctly
+// rounded.
 //
 // A causal flag replaces causal_mask()'s additive -1e9 entries without
 // reading them: those keys get an exponential of exactly 0, so leaving them
 // out of the max, the sum and the weighted sum of v changes no bit (adding
 // +-0 to a non-zero fp32 sum is exact, and the diagonal key keeps every row's
-// sum non-zero).
+// sum non-zero).  For the same reason the diagonal tile skips, in both
+// products, the groups of 16 rows that lie wholly before a group of keys.
 //
 // Work decomposition: one CTA per (batch, head, block of 64 query rows), the
 // blocks with the most keys (causal) first.  The CTA stages its query rows,
-// then 64-key tiles of K, in shared memory (row pitch d_k + 4 floats, so the
-// 16-byte reads of 8 consecutive lanes fall in distinct bank groups), keeps
-// the block's whole score rows on chip, runs the softmax there and streams
-// 64-key tiles of V for the weighted sum.  256 threads, thread tile 4 query
-// rows x 4 keys (row pairs ty + 16 rp of rows i, i + 8; keys tx + 16 c).  The
-// sums run on sm_100's packed f32x2 add, one instruction per two rows, each
-// half rounded as the scalar instruction would (the products are scalar
-// multiplies): query rows and score rows are stored pair-interleaved so their
-// 16-byte loads give both rows' operands, and per 4 reduction steps 8 shared
-// loads feed 96 instructions (128 fp32 operations).  The next tile's global
-// loads are issued into registers before the current tile's arithmetic.  The output is written
-// head-merged ([batch, seq_q, heads * d_k], the layout the output projection
-// reads) with the absmax partials of every value, so the projection's
-// per-tensor quantize needs no extra pass.
+// then 64-key tiles of K, in shared memory (K / V rows at a pitch of d_k + 4
+// floats, so the 16-byte reads of 8 consecutive lanes fall in distinct bank
+// groups), keeps the block's whole score rows on chip, runs the softmax there
+// and streams 64-key tiles of V for the weighted sum.  256 threads, thread
+// tile 4 query rows x 4 keys (row pairs ty + 16 rp of rows i, i + 8; keys
+// tx + 16 c).  The sums run on sm_100's packed f32x2 add, one instruction per
+// two rows, each half rounded as the scalar instruction would (the products
+// are scalar multiplies): query rows and score rows are stored
+// pair-interleaved so their 16-byte loads give both rows' operands, and per 4
+// reduction steps 8 shared loads feed 96 instructions (128 fp32 operations).
+// The next tile's global loads are issued into registers before the current
+// tile's arithmetic.  The output is written head-merged ([batch, seq_q,
+// heads * d_k], the layout the output projection reads) with the absmax
+// partials of every value, so the projection's per-tensor quantize needs no
+// extra pass.
 #include <math.h>
 
 #include <algorithm>
