@@ -564,21 +564,18 @@ __global__ void __launch_bounds__(kResidentBlock, 1)
 // for bit.  NULL gamma / beta act as the reference's initial ones / zeros
 // (the + 0.0f still turns a -0.0 into +0.0, as the reference's add does).
 //
-// A block owns kLnRows rows, each of its four warps kLnRowsPerWarp of them.
-// Staged form (D % 4 == 0, 16-byte aligned rows, kLnRows rows fit in shared
-// memory): a warp copies its rows in with coalesced 16-byte loads (adding the
-// residual and writing the sum when there is one), then its lane r walks row
-// r serially from shared memory -- the sums must run in index order, and one
-// thread per row keeps the order without a cross-lane combine -- reading 16
-// bytes at a time (the row pitch is 16 bytes times an odd number modulo 128,
-// so lanes reading different rows hit distinct bank groups), and finally the
-// warp writes y with coalesced 16-byte stores and takes its absmax.  The
-// warps synchronise only within themselves, so one warp's copies overlap
-// another's ordered sums.  Otherwise the same arithmetic reads global memory
-// directly.
+// A block owns kLnRows rows.  Staged form (D % 4 == 0, 16-byte aligned rows,
+// kLnRows rows fit in shared memory): all threads copy the rows in with
+// coalesced 16-byte loads (adding the residual and writing the sum when there
+// is one), then lane r of warp 0 walks row r serially from shared memory --
+// the sums must run in index order, and one thread per row keeps the order
+// without a cross-lane combine -- reading 16 bytes at a time (the row pitch
+// is 16 bytes times an odd number modulo 128, so the eight lanes of each
+// quarter-warp hit distinct bank groups), and finally all threads write y with
+// coalesced 16-byte stores and take its absmax.  Otherwise the same
+// arithmetic reads global memory directly.
 constexpr int kLnRows = 16;
 constexpr int kLnThreads = 128;
-constexpr int kLnRowsPerWarp = kLnRows / (kLnThreads / 32);   // 4
 constexpr int kLnBatch = 8;   // 16-byte loads in flight per thread while staging rows
 
 __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
@@ -597,24 +594,17 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
     for (int64_t r0 = (int64_t)blockIdx.x * kLnRows; r0 < M; r0 += (int64_t)gridDim.x * kLnRows) {
         const int rows = (int)min((int64_t)kLnRows, M - r0);
         if (staged) {
-            // each warp owns rows 4 warp .. 4 warp + 3 of the group and runs its
-            // own stage -> ordered sums -> output cycle (warp barriers only), so
-            // one warp's loads and stores overlap another's serial sums
+            // rows in: ln_rows[r * stride + j] = x (+ res); batches of kLnBatch
+            // 16-byte loads per thread are issued before any is used
             const int d4 = (int)D4;
-            const int wr0 = kLnRowsPerWarp * warp;
-            const int wrows = max(0, min(kLnRowsPerWarp, rows - wr0));
-            const int total = wrows * d4;
-            const int64_t g0 = (r0 + wr0) * D4;   // first float4 of the warp's rows
-            const float4* x4 = reinterpret_cast<const float4*>(x) + g0;
-            const float4* res4 = res ? reinterpret_cast<const float4*>(res) + g0 : nullptr;
-            float* wrow = ln_rows + (int64_t)wr0 * stride;
-            // rows in: wrow[r * stride + j] = x (+ res); kLnBatch 16-byte loads per
-            // lane are issued before any is used
-            for (int t0 = lane; t0 < total; t0 += 32 * kLnBatch) {
+            const int total = rows * d4;
+            const float4* x4 = reinterpret_cast<const float4*>(x) + r0 * D4;
+            const float4* res4 = res ? reinterpret_cast<const float4*>(res) + r0 * D4 : nullptr;
+            for (int t0 = threadIdx.x; t0 < total; t0 += kLnThreads * kLnBatch) {
                 float4 v[kLnBatch], w[kLnBatch];
 #pragma unroll
                 for (int u = 0; u < kLnBatch; ++u) {
-                    const int t = t0 + u * 32;
+                    const int t = t0 + u * kLnThreads;
                     if (t < total) {
                         v[u] = __ldg(x4 + t);
                         if (res4) w[u] = __ldg(res4 + t);
@@ -622,7 +612,7 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
                 }
 #pragma unroll
                 for (int u = 0; u < kLnBatch; ++u) {
-                    const int t = t0 + u * 32;
+                    const int t = t0 + u * kLnThreads;
                     if (t < total) {
                         const int r = t / d4;
                         const int c = t - r * d4;
@@ -632,15 +622,15 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
                             a.y = __fadd_rn(a.y, w[u].y);
                             a.z = __fadd_rn(a.z, w[u].z);
                             a.w = __fadd_rn(a.w, w[u].w);
-                            reinterpret_cast<float4*>(sum_out)[g0 + t] = a;
+                            reinterpret_cast<float4*>(sum_out)[r0 * D4 + t] = a;
                         }
-                        *reinterpret_cast<float4*>(wrow + (int64_t)r * stride + 4 * c) = a;
+                        *reinterpret_cast<float4*>(ln_rows + (int64_t)r * stride + 4 * c) = a;
                     }
                 }
             }
-            __syncwarp();
-            if (lane < wrows) {
-                const float4* row = reinterpret_cast<const float4*>(wrow + (int64_t)lane * stride);
+            __syncthreads();
+            if (warp == 0 && lane < rows) {
+                const float4* row = reinterpret_cast<const float4*>(ln_rows + (int64_t)lane * stride);
                 float s = 0.0f;
 #pragma unroll 8
                 for (int c = 0; c < d4; ++c) {
@@ -659,15 +649,15 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
                     q = __fadd_rn(q, __fmul_rn(e, e));
                     q = __fadd_rn(q, __fmul_rn(f, f));
                 }
-                s_mean[wr0 + lane] = mean;
-                s_rden[wr0 + lane] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(q, inv_d), eps)));
+                s_mean[lane] = mean;
+                s_rden[lane] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(q, inv_d), eps)));
             }
-            __syncwarp();
-            for (int t = lane; t < total; t += 32) {
+            __syncthreads();
+            for (int t = threadIdx.x; t < rows * d4; t += kLnThreads) {
                 const int r = t / d4;
                 const int c = t - r * d4;
-                const float mean = s_mean[wr0 + r], rden = s_rden[wr0 + r];
-                const float4 v = *reinterpret_cast<const float4*>(wrow + (int64_t)r * stride + 4 * c);
+                const float mean = s_mean[r], rden = s_rden[r];
+                const float4 v = *reinterpret_cast<const float4*>(ln_rows + (int64_t)r * stride + 4 * c);
                 const float4 gm = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + c) : make_float4(1.f, 1.f, 1.f, 1.f);
                 const float4 bt = beta ? __ldg(reinterpret_cast<const float4*>(beta) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
                 float4 o;
@@ -675,10 +665,10 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_partials_kernel(
                 o.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mean), rden), gm.y), bt.y);
                 o.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mean), rden), gm.z), bt.z);
                 o.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mean), rden), gm.w), bt.w);
-                reinterpret_cast<float4*>(y)[g0 + t] = o;
+                reinterpret_cast<float4*>(y)[(r0 + r) * D4 + c] = o;
                 m = max(m, max(max(abs_bits(o.x), abs_bits(o.y)), max(abs_bits(o.z), abs_bits(o.w))));
             }
-            __syncwarp();   // the warp's rows and statistics are reused by its next row group
+            __syncthreads();   // ln_rows and the row statistics are reused by the next row group
         } else {
             auto val = [&](int64_t i) { return res ? __fadd_rn(x[i], res[i]) : x[i]; };
             if (warp == 0 && lane < rows) {
