@@ -98,6 +98,47 @@ def test_dequantize_form_query():
         assert lib.kz_dequantize_uses_table(s) == 1, s
 
 
+def _f32_rn(v):
+    """The fp32 nearest to the exact rational v (ties to even)."""
+    import numpy as np
+    from fractions import Fraction
+    f = np.float32(float(v))
+    best = None
+    for c in (np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))):
+        d = abs(Fraction(float(c)) - v)
+        key = (d, int(np.asarray(c).view(np.uint32)) & 1)   # on a tie the even significand wins
+        if best is None or key < best[0]:
+            best = (key, c)
+    return best[1]
+
+
+def test_dequantize_split_predicate_against_exact_arithmetic():
+    """The host's choice of the table-free dequantize is pinned to exact
+    rational arithmetic: for random scales, the split form fma(q, s_hi,
+    fl(q * s_lo)) -- evaluated here exactly and rounded once -- equals
+    (float)((double)q * scale) for every byte value exactly when the library
+    says so."""
+    import numpy as np
+    from fractions import Fraction
+    lib = _lib.load()
+    rs = np.random.RandomState(11)
+    scales = list(rs.uniform(1e-6, 2.0, 150)) + list(10.0 ** rs.uniform(-30, 30, 50)) + [3e-39, 1e-42, -0.25]
+    for s in scales:
+        s = float(s)
+        hi = np.float32(s)
+        lo = np.float32(np.float64(s) - np.float64(hi))
+        ok = bool(np.isfinite(hi) and np.isfinite(lo))
+        for c in range(-128, 128):
+            if not ok:
+                break
+            exact = np.float32(np.float64(c) * s)
+            p = np.float32(np.float32(c) * lo)
+            cand = _f32_rn(Fraction(c) * Fraction(float(hi)) + Fraction(float(p)))
+            if np.asarray(exact).view(np.uint32) != np.asarray(cand).view(np.uint32):
+                ok = False
+        assert lib.kz_dequantize_uses_table(s) == (0 if ok else 1), s
+
+
 def test_exchange_entry_points_validate_arguments_without_gpu():
     """The overlapped-exchange entry points reject bad arguments before any
     device work, with a message."""
