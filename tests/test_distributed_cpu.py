@@ -414,11 +414,14 @@ def _pipe2d_worker(rank, world, port, q, tp):
         q.put((rank, repr(e)))
 
 
-def test_pipelined_stack_row_groups_world4_gloo_matches_oracle_chain():
-    """Four gloo ranks as two row groups of two column shards (tp=2): each
-    group runs the pipelined forward on half the rows, the absmax is
-    all-reduced over all four ranks, and the gathered output equals the
-    oracle's unsharded chain; the four ranks' input rows tile the batch."""
+@pytest.mark.parametrize("world,tp", [(4, 2), (2, 1)])
+def test_pipelined_stack_row_groups_gloo_matches_oracle_chain(world, tp):
+    """gloo ranks as row groups of column shards -- four ranks as two groups
+    of two (tp=2), and two ranks as two groups of one (tp=1: each rank holds
+    whole weights and half the rows, the one exchange the absmax): each group
+    runs the pipelined forward on its rows, the absmax is all-reduced over all
+    ranks, and the gathered output equals the oracle's unsharded chain; the
+    ranks' input rows tile the batch."""
     from oracle import cpu as ocpu
     a, s_a = ocpu.quantize_tensor(_pipe_x())
     want = None
@@ -430,17 +433,17 @@ def test_pipelined_stack_row_groups_world4_gloo_matches_oracle_chain():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_pipe2d_worker, args=(r, 4, port, q, 2)) for r in range(4)]
+    procs = [ctx.Process(target=_pipe2d_worker, args=(r, world, port, q, tp)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(4):
+    for _ in range(world):
         r, v = q.get(timeout=300)
         res[r] = v
     for p in procs:
         p.join(timeout=60)
     covered = []
-    for r in range(4):
+    for r in range(world):
         assert isinstance(res[r], tuple), res[r]
         y, rows = res[r]
         assert y.tobytes() == want.tobytes()
